@@ -1,0 +1,130 @@
+/*
+ * kotflash_b200 — C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers, sizes and element
+ * strides, launches on the caller's CUDA stream, never allocates device
+ * memory, never synchronises, and returns a status code (KF_OK == 0).  On a
+ * non-zero status `kf_last_error()` returns a thread-local message.
+ *
+ * Tensors are described by `kf_tensor4`: a [n0, n1, n2, n3] strided view
+ * (strides in ELEMENTS, like torch.Tensor.stride()).  Attention tensors use
+ * the reference's [batch, heads, sequence, head_dim] layout
+ * (kotflash/attention.py:232-236).  Element types are fp16 or bf16
+ * (`KF_F16`, `KF_BF16`); LSE, partials and gradient workspaces are fp32.
+ *
+ * Device-side waits are bounded.  Kernels that give up on a wait write a
+ * non-zero code into the caller-supplied `status` word (int32 in device
+ * memory) and return; the host reads that word outside the hot path.
+ */
+#ifndef KOTFLASH_B200_H
+#define KOTFLASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define KF_OK              0
+#define KF_ERR_INVALID     1  /* bad argument (shape, stride, alignment)     */
+#define KF_ERR_UNSUPPORTED 2  /* valid but outside this build's envelope     */
+#define KF_ERR_CUDA        3  /* a CUDA runtime/driver call failed           */
+#define KF_ERR_WORKSPACE   4  /* workspace pointer/size too small            */
+
+/* device status word values written by kernels */
+#define KF_DEV_OK          0
+#define KF_DEV_TIMEOUT     1  /* a bounded mbarrier wait expired             */
+
+#define KF_F16  0
+#define KF_BF16 1
+
+typedef struct kf_tensor4 {
+  void*   ptr;
+  int64_t size[4];
+  int64_t stride[4];
+} kf_tensor4;
+
+/* ---- version / errors -------------------------------------------------- */
+int         kf_version(void);
+const char* kf_last_error(void);
+
+/* ---- K4: KV-cache append ------------------------------------------------
+ * Replaces the pybind op `append_kv_(k_cache, v_cache, new_k, new_v, start)`
+ * (kotflash/csrc/kv_append.cpp:11-14) and its host checks + launch
+ * (kotflash/csrc/kv_append_cuda.cu:44-96).  Copies new_k/new_v [B,H,S,D] into
+ * k_cache/v_cache [B,H,cap,D] at sequence offset `start`, K and V in ONE
+ * launch.  Bit-exact (pure data movement).  Unlike the reference, fp16 and
+ * bf16 are accepted and the destination may be any strided view whose last
+ * dimension is contiguous. */
+int kf_append(const kf_tensor4* k_cache, const kf_tensor4* v_cache,
+              const kf_tensor4* new_k, const kf_tensor4* new_v,
+              int64_t start, int dtype, void* stream);
+
+/* ---- K1: forward --------------------------------------------------------
+ * Replaces `attention_forward(q, k, v, causal, scale) -> (out, lse)`
+ * (kotflash/kernels/triton_forward.py:372-456) and the kernel
+ * `_attention_fwd_kernel` (triton_forward.py:21-165).  Writes O [B,Hq,Sq,D]
+ * (q dtype) and LSE [B,Hq,Sq] fp32 (natural log of the row's softmax
+ * denominator over scale*QK^T).  Causal masks are upper-left aligned (key
+ * j visible to query i iff j <= i).  Requirements: 16 <= D <= 128, D % 8 == 0,
+ * last-dim-contiguous tensors with 16-byte aligned base and strides; O and
+ * LSE contiguous. */
+int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                const kf_tensor4* o, float* lse, int dtype, float scale,
+                int causal, int32_t* status, void* stream);
+
+/* ---- K2: backward -------------------------------------------------------
+ * Replaces `attention_backward(q, k, v, out, lse, grad_out, causal, scale)`
+ * (kotflash/kernels/triton_backward.py:335-421) and its kernels
+ * `_attention_bwd_dq`, `_attention_bwd_dkv(_split)`, `_attention_bwd_dkv_reduce`
+ * (triton_backward.py:18-332).  Writes dq, dk, dv (input dtype) given the
+ * forward's O and LSE and the upstream gradient dO.  dK/dV sum over the
+ * GQA group of each KV head.  `workspace` must hold
+ * kf_attn_bwd_workspace_bytes(...) bytes (fp32 dQ accumulator + row deltas). */
+size_t kf_attn_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D);
+int kf_attn_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                const kf_tensor4* o, const float* lse, const kf_tensor4* dout,
+                const kf_tensor4* dq, const kf_tensor4* dk, const kf_tensor4* dv,
+                int dtype, float scale, int causal,
+                void* workspace, size_t workspace_bytes,
+                int32_t* status, void* stream);
+
+/* ---- K3: split-KV decode ------------------------------------------------
+ * Replaces `attention_forward_strided_decode(q, k, v, scale)`
+ * (kotflash/kernels/triton_decode.py:412-468; kernels `_strided_decode_split`
+ * 17-104 and `_strided_decode_reduce` 242-297), the split-KV branch of
+ * `attention_forward` (triton_forward.py:410-445; kernels 170-349), and, when
+ * new_k/new_v are non-NULL, the fused one-token append
+ * `attention_forward_strided_append` (triton_decode.py:302-386): the new row
+ * is written at position `past_len` of the cache and attended in the same
+ * pass.  Non-causal, Sq <= 16.  K/V may be strided prefix views of a larger
+ * cache (last dim contiguous).  Writes O (q dtype) and, if lse != NULL, the
+ * merged LSE.  num_splits == 0 lets the planner choose.
+ * `workspace` must hold kf_decode_workspace_bytes(...) bytes. */
+int    kf_decode_num_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                            int64_t Sk, int64_t D, int sm_count);
+size_t kf_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D,
+                                 int num_splits);
+int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+              const kf_tensor4* new_k, const kf_tensor4* new_v, int64_t past_len,
+              const kf_tensor4* o, float* lse, int dtype, float scale,
+              int num_splits, void* workspace, size_t workspace_bytes,
+              void* stream);
+
+/* ---- K3b: LSE-weighted merge of partial (O, LSE) ------------------------
+ * Replaces `_attention_fwd_split_kv_reduce` (triton_forward.py:270-349).
+ * part_o: [S, rows, D] fp32, part_lse: [S, rows] fp32, where rows =
+ * B*Hq*Sq in [b][h][s] order.  Writes o (rows x D, dtype, contiguous) and,
+ * if lse != NULL, the merged LSE.  Empty partials carry LSE = -inf and
+ * contribute nothing; a row whose partials are all empty yields O = 0 and
+ * LSE = -inf.  Used for the cross-GPU merge after the all-gather. */
+int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits,
+                      int64_t rows, int64_t D, void* o, float* lse, int dtype,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KOTFLASH_B200_H */

@@ -1,0 +1,98 @@
+// Library-wide C-ABI pieces: version, thread-local error text, TMA descriptor
+// encoding and the device-property cache.
+#include <mutex>
+#include <string>
+
+#include "kf_host.h"
+
+namespace kf {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return set_error(KF_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return KF_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+int encode_tmap_4d(CUtensorMap* map, const kf_tensor4* t, int box_inner, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return set_error(KF_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (t->stride[3] != 1) return set_error(KF_ERR_INVALID, "TMA view needs a contiguous last dim");
+  if (!aligned16(t->ptr)) return set_error(KF_ERR_INVALID, "TMA base pointer not 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)t->size[3], (cuuint64_t)t->size[2], (cuuint64_t)t->size[1],
+                        (cuuint64_t)t->size[0]};
+  cuuint64_t strides[3] = {(cuuint64_t)t->stride[2] * 2, (cuuint64_t)t->stride[1] * 2,
+                           (cuuint64_t)t->stride[0] * 2};
+  for (int i = 0; i < 3; ++i) {
+    if (strides[i] % 16 != 0 || strides[i] == 0) {
+      // a size-1 dimension may carry any stride; give it a legal one
+      const int dim = 3 - 1 - i;  // strides[i] belongs to size[2 - i]
+      if (t->size[dim] == 1) {
+        strides[i] = (i == 0 ? dims[0] * 2 : strides[i - 1] * dims[i]);
+        strides[i] = (strides[i] + 15) / 16 * 16;
+      } else {
+        return set_error(KF_ERR_INVALID, "TMA stride %llu bytes is not a multiple of 16",
+                         (unsigned long long)strides[i]);
+      }
+    }
+  }
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, t->ptr, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KF_OK;
+}
+
+int sm_count_current_device() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace kf
+
+extern "C" int kf_version(void) { return 10000; }  // 1.0.0
+
+extern "C" const char* kf_last_error(void) { return kf::g_last_error.c_str(); }

@@ -1,0 +1,572 @@
+// K3: split-KV decode for short queries (Sq <= 16) over long, possibly strided
+// K/V, plus K3b, the LSE-weighted merge of split partials.
+//
+// Replaces the reference's `_attention_fwd_split_kv` + `_attention_fwd_split_kv_reduce`
+// (kotflash/kernels/triton_forward.py:170-349), `_strided_decode_split` +
+// `_strided_decode_reduce` (kotflash/kernels/triton_decode.py:17-104, 242-297)
+// and the fused one-token append `_strided_decode_append_split`
+// (triton_decode.py:109-238).
+//
+// Design (HBM-bound):
+//  * one CTA per (split, batch, KV head, row block): all GROUP x Sq query rows
+//    that share a KV head are packed into one tile, so each K/V byte of the
+//    split is read from HBM exactly once (the reference reads it once per
+//    query head);
+//  * each of the 4 warps streams its own 16-key tiles (every 4th tile of the
+//    split) through a private cp.async ring of 16-byte loads into XOR-swizzled
+//    shared memory, so warps never wait on one another inside the loop;
+//  * QK^T and PV use warp-level m16n8k16 MMAs (ldmatrix operands) with an
+//    online softmax in the exp2 domain; the 4 warps' (m, l, O) are merged in
+//    shared memory at the end;
+//  * with one split the CTA writes O/LSE directly, otherwise fp32 partials
+//    (O normalised, LSE natural log) that the merge kernel combines.
+#include <math.h>
+
+#include "kf_host.h"
+#include "kf_sm100.cuh"
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTileKeys = 16;  // keys per warp tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct DecodeArgs {
+  const uint16_t* q;
+  const uint16_t* k;
+  const uint16_t* v;
+  const uint16_t* nk;  // fused-append source rows (null when not fused)
+  const uint16_t* nv;
+  uint16_t* kw;  // cache base for the fused append write
+  uint16_t* vw;
+  uint16_t* o;
+  float* lse;
+  float* part_o;
+  float* part_lse;
+  int64_t qs[4], ks[4], vs[4], nks[4], nvs[4], os[4];
+  int B, Hq, Hkv, G, Sq, Sk, D;
+  int64_t past_len;
+  int num_splits, chunk;
+  int rows;  // G * Sq packed rows per KV head
+  int64_t prow_total;  // B * Hq * Sq
+  float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
+  return (uint32_t)(row * row_bytes + ((((chunk & 7) ^ (row & 7)) | (chunk & ~7)) << 4));
+}
+
+__device__ __forceinline__ float warp_max4(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+  return x;
+}
+
+template <bool BF16, int DP, int MT, int STAGES>
+__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs a) {
+  constexpr int ROWS = MT * 16;
+  constexpr int ROW_BYTES = DP * 2;
+  constexpr int CHUNKS = DP / 8;  // 16-byte chunks per row
+  constexpr int TILE_BYTES = kTileKeys * ROW_BYTES;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + ROWS * ROW_BYTES;  // [warp][stage][K|V][16][DP]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x;
+  const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  const int row0 = blockIdx.z * ROWS;
+  const int key_begin = split * a.chunk;
+  const int key_end = min(key_begin + a.chunk, a.Sk);
+  const bool fused = a.nk != nullptr;
+
+  // fused append: the CTA of the split owning the new position (row block 0)
+  // writes the new K/V row into the cache; every CTA reads it from nk/nv.
+  if (fused && blockIdx.z == 0 && a.past_len >= key_begin && a.past_len < key_end && warp == 0) {
+    for (int c = lane; c < a.D / 8; c += 32) {
+      const uint4 kv = *reinterpret_cast<const uint4*>(a.nk + b * a.nks[0] + kvh * a.nks[1] + c * 8);
+      const uint4 vv = *reinterpret_cast<const uint4*>(a.nv + b * a.nvs[0] + kvh * a.nvs[1] + c * 8);
+      *reinterpret_cast<uint4*>(a.kw + b * a.ks[0] + kvh * a.ks[1] + a.past_len * a.ks[2] + c * 8) = kv;
+      *reinterpret_cast<uint4*>(a.vw + b * a.vs[0] + kvh * a.vs[1] + a.past_len * a.vs[2] + c * 8) = vv;
+    }
+  }
+
+  // ---- Q tile (packed rows), zero-filled outside [rows) x [D)
+  for (int i = tid; i < ROWS * CHUNKS; i += kThreads) {
+    const int r = i / CHUNKS, c = i % CHUNKS;
+    const int pr = row0 + r;
+    const bool ok = pr < a.rows && c * 8 < a.D;
+    const int g = ok ? pr / a.Sq : 0, s = ok ? pr % a.Sq : 0;
+    const uint16_t* src = a.q + b * a.qs[0] + (int64_t)(kvh * a.G + g) * a.qs[1] + s * a.qs[2] + (ok ? c * 8 : 0);
+    kf::cp_async16(sQ + swz(r, c, ROW_BYTES), src, ok);
+  }
+  kf::cp_async_commit();
+  kf::cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- per-warp pipeline over 16-key tiles j = warp, warp+4, ...
+  const int n_tiles = (key_end - key_begin + kTileKeys - 1) / kTileKeys;
+  const int n_my = n_tiles > warp ? (n_tiles - warp + kWarps - 1) / kWarps : 0;
+  uint8_t* my_ring = sKV + warp * STAGES * 2 * TILE_BYTES;
+  const uint16_t* kbase = a.k + b * a.ks[0] + kvh * a.ks[1];
+  const uint16_t* vbase = a.v + b * a.vs[0] + kvh * a.vs[1];
+
+  auto load_tile = [&](int it, int stage) {
+    const int key0 = key_begin + (warp + it * kWarps) * kTileKeys;
+    uint8_t* sk = my_ring + stage * 2 * TILE_BYTES;
+    uint8_t* sv = sk + TILE_BYTES;
+#pragma unroll
+    for (int i = lane; i < kTileKeys * CHUNKS; i += 32) {
+      const int r = i / CHUNKS, c = i % CHUNKS;
+      const int key = key0 + r;
+      const bool ok = key < key_end && c * 8 < a.D;
+      const uint16_t* ks;
+      const uint16_t* vs;
+      if (fused && key == a.past_len) {
+        ks = a.nk + b * a.nks[0] + kvh * a.nks[1];
+        vs = a.nv + b * a.nvs[0] + kvh * a.nvs[1];
+      } else {
+        ks = kbase + (int64_t)(ok ? key : key_begin) * a.ks[2];
+        vs = vbase + (int64_t)(ok ? key : key_begin) * a.vs[2];
+      }
+      kf::cp_async16(sk + swz(r, c, ROW_BYTES), ks + (ok ? c * 8 : 0), ok);
+      kf::cp_async16(sv + swz(r, c, ROW_BYTES), vs + (ok ? c * 8 : 0), ok);
+    }
+  };
+
+  float m_run[MT][2], l_run[MT][2];
+  float o_acc[MT][DP / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    m_run[mt][0] = m_run[mt][1] = -INFINITY;
+    l_run[mt][0] = l_run[mt][1] = 0.f;
+#pragma unroll
+    for (int n = 0; n < DP / 8; ++n) o_acc[mt][n][0] = o_acc[mt][n][1] = o_acc[mt][n][2] = o_acc[mt][n][3] = 0.f;
+  }
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < n_my) load_tile(s, s);
+    kf::cp_async_commit();
+  }
+  const uint32_t sQ_u = kf::smem_u32(sQ);
+  for (int it = 0; it < n_my; ++it) {
+    if (it + STAGES - 1 < n_my) load_tile(it + STAGES - 1, (it + STAGES - 1) % STAGES);
+    kf::cp_async_commit();
+    kf::cp_async_wait<STAGES - 1>();
+    __syncwarp();
+    const uint32_t sk_u = kf::smem_u32(my_ring + (it % STAGES) * 2 * TILE_BYTES);
+    const uint32_t sv_u = sk_u + TILE_BYTES;
+    const int key0 = key_begin + (warp + it * kWarps) * kTileKeys;
+
+    // S = Q K^T for 16 keys
+    float sc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int n = 0; n < 2; ++n) sc[mt][n][0] = sc[mt][n][1] = sc[mt][n][2] = sc[mt][n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < DP / 16; ++kk) {
+      uint32_t kb[4];
+      kf::ldmatrix_x4(kb, sk_u + swz((lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), ROW_BYTES));
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t qa[4];
+        kf::ldmatrix_x4(qa, sQ_u + swz(mt * 16 + (lane & 15), 2 * kk + (lane >> 4), ROW_BYTES));
+        kf::mma_16816<BF16>(sc[mt][0], qa, kb[0], kb[1]);
+        kf::mma_16816<BF16>(sc[mt][1], qa, kb[2], kb[3]);
+      }
+    }
+
+    // online softmax (log2 domain), then O += P V
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      uint32_t pa[4];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float x[4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = key0 + n * 8 + 2 * (lane & 3) + e;
+            x[n * 2 + e] = key < key_end ? sc[mt][n][half * 2 + e] * a.scale_log2 : -INFINITY;
+          }
+        const float mx = warp_max4(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
+        const float m_new = fmaxf(m_run[mt][half], mx);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = kf::ex2(m_run[mt][half] - m_use);
+        float p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = kf::ex2(x[j] - m_use);
+        l_run[mt][half] = l_run[mt][half] * alpha + (p[0] + p[1] + p[2] + p[3]);
+        m_run[mt][half] = m_new;
+#pragma unroll
+        for (int n = 0; n < DP / 8; ++n) {
+          o_acc[mt][n][half * 2 + 0] *= alpha;
+          o_acc[mt][n][half * 2 + 1] *= alpha;
+        }
+        pa[half] = kf::pack2<BF16>(p[0], p[1]);      // keys 0-7 of the tile
+        pa[2 + half] = kf::pack2<BF16>(p[2], p[3]);  // keys 8-15
+      }
+#pragma unroll
+      for (int dn = 0; dn < DP / 16; ++dn) {
+        uint32_t vb[4];
+        kf::ldmatrix_x4_trans(vb, sv_u + swz(lane & 15, 2 * dn + (lane >> 4), ROW_BYTES));
+        kf::mma_16816<BF16>(o_acc[mt][2 * dn], pa, vb[0], vb[1]);
+        kf::mma_16816<BF16>(o_acc[mt][2 * dn + 1], pa, vb[2], vb[3]);
+      }
+    }
+    __syncwarp();
+  }
+  kf::cp_async_wait<0>();
+
+  // ---- merge the 4 warps in shared memory (reuses the pipeline buffers)
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float l = l_run[mt][half];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      l_run[mt][half] = l;
+    }
+  __syncthreads();
+  float* ml = reinterpret_cast<float*>(smem);          // [warp][ROWS][2]
+  float* row_w = ml + kWarps * ROWS * 2;               // [warp][ROWS] weights
+  float* row_lse = row_w + kWarps * ROWS;              // [ROWS]
+  float* obuf = row_lse + ROWS;                        // [warp][ROWS][DP]
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = mt * 16 + (lane >> 2) + half * 8;
+      if ((lane & 3) == 0) {
+        ml[(warp * ROWS + r) * 2 + 0] = m_run[mt][half];
+        ml[(warp * ROWS + r) * 2 + 1] = l_run[mt][half];
+      }
+#pragma unroll
+      for (int n = 0; n < DP / 8; ++n) {
+        const int c = n * 8 + 2 * (lane & 3);
+        obuf[(warp * ROWS + r) * DP + c] = o_acc[mt][n][half * 2];
+        obuf[(warp * ROWS + r) * DP + c + 1] = o_acc[mt][n][half * 2 + 1];
+      }
+    }
+  __syncthreads();
+  if (tid < ROWS) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ml[(w * ROWS + tid) * 2]);
+    float L = 0.f, wt[kWarps];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = ml[(w * ROWS + tid) * 2];
+      wt[w] = (M == -INFINITY) ? 0.f : kf::ex2(mw - M);
+      L += wt[w] * ml[(w * ROWS + tid) * 2 + 1];
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) row_w[w * ROWS + tid] = wt[w] * inv;
+    row_lse[tid] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+  }
+  __syncthreads();
+
+  const int64_t prow_base = (int64_t)(b * a.Hkv + kvh) * a.rows + row0;
+  const int valid_rows = min(ROWS, a.rows - row0);
+  for (int i = tid; i < valid_rows * (DP / 4); i += kThreads) {
+    const int r = i / (DP / 4), c4 = (i % (DP / 4)) * 4;
+    if (c4 >= a.D) continue;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float wt = row_w[w * ROWS + r];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += wt * obuf[(w * ROWS + r) * DP + c4 + e];
+    }
+    const int pr = row0 + r;
+    if (a.num_splits == 1) {
+      const int g = pr / a.Sq, s = pr % a.Sq;
+      uint16_t* dst = a.o + b * a.os[0] + (int64_t)(kvh * a.G + g) * a.os[1] + s * a.os[2] + c4;
+      const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
+      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+    } else {
+      float* dst = a.part_o + ((int64_t)split * a.prow_total + prow_base + r) * a.D + c4;
+      *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+  }
+  if (tid < valid_rows) {
+    if (a.num_splits == 1) {
+      if (a.lse) a.lse[prow_base + tid] = row_lse[tid];
+    } else {
+      a.part_lse[(int64_t)split * a.prow_total + prow_base + tid] = row_lse[tid];
+    }
+  }
+}
+
+// K3b: one warp per output row merges S partials by their LSE weights.
+struct MergeArgs {
+  const float* part_o;
+  const float* part_lse;
+  int S;
+  int64_t rows;
+  int D;
+  uint16_t* o;
+  float* lse;
+  int Hq, Sq;
+  int64_t os0, os1, os2;
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(128) merge_kernel(const MergeArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  if (row >= a.rows) return;
+  float mx = -INFINITY;
+  for (int s = lane; s < a.S; s += 32) mx = fmaxf(mx, a.part_lse[(int64_t)s * a.rows + row]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  float den = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = lane; s < a.S; s += 32)
+      den += kf::ex2((a.part_lse[(int64_t)s * a.rows + row] - mx) * kLog2e);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const int c4 = lane * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (c4 < a.D && den > 0.f) {
+    for (int s = 0; s < a.S; ++s) {
+      const float ls = a.part_lse[(int64_t)s * a.rows + row];
+      if (ls == -INFINITY) continue;
+      const float w = kf::ex2((ls - mx) * kLog2e) * inv;
+      const float4 p = *reinterpret_cast<const float4*>(a.part_o + ((int64_t)s * a.rows + row) * a.D + c4);
+      acc[0] += w * p.x;
+      acc[1] += w * p.y;
+      acc[2] += w * p.z;
+      acc[3] += w * p.w;
+    }
+  }
+  if (c4 < a.D) {
+    const int64_t bh = row / a.Sq;
+    const int64_t s_ = row % a.Sq;
+    const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
+    uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + c4;
+    const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+  }
+  if (lane == 0 && a.lse) a.lse[row] = den > 0.f ? mx + logf(den) : -INFINITY;
+}
+
+template <bool BF16>
+int launch_merge(const MergeArgs& m, cudaStream_t st) {
+  const unsigned blocks = (unsigned)((m.rows + 3) / 4);
+  merge_kernel<BF16><<<blocks, 128, 0, st>>>(m);
+  return kf::check_launch("kf merge");
+}
+
+template <bool BF16, int DP, int MT>
+int launch_split(const DecodeArgs& a, int row_blocks, cudaStream_t st) {
+  constexpr int STAGES = DP == 64 ? 4 : 3;
+  constexpr int ROWS = MT * 16;
+  const size_t pipe = (size_t)ROWS * DP * 2 + (size_t)kWarps * STAGES * 2 * kTileKeys * DP * 2;
+  const size_t merge = (size_t)kWarps * ROWS * 3 * 4 + ROWS * 4 + (size_t)kWarps * ROWS * DP * 4;
+  const size_t smem = pipe > merge ? pipe : merge;
+  auto kern = decode_split_kernel<BF16, DP, MT, STAGES>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
+  dim3 grid(a.num_splits, a.B * a.Hkv, row_blocks);
+  kern<<<grid, kThreads, smem, st>>>(a);
+  return kf::check_launch("kf_decode");
+}
+
+template <bool BF16>
+int dispatch_split(const DecodeArgs& a, cudaStream_t st) {
+  const int dp = a.D <= 64 ? 64 : 128;
+  const int mt_max = dp == 64 ? 4 : 2;
+  int mt = (a.rows + 15) / 16;
+  if (mt > mt_max) mt = mt_max;
+  const int row_blocks = (a.rows + mt * 16 - 1) / (mt * 16);
+  if (dp == 64) {
+    switch (mt) {
+      case 1: return launch_split<BF16, 64, 1>(a, row_blocks, st);
+      case 2: return launch_split<BF16, 64, 2>(a, row_blocks, st);
+      case 3: return launch_split<BF16, 64, 3>(a, row_blocks, st);
+      default: return launch_split<BF16, 64, 4>(a, row_blocks, st);
+    }
+  }
+  if (mt == 1) return launch_split<BF16, 128, 1>(a, row_blocks, st);
+  return launch_split<BF16, 128, 2>(a, row_blocks, st);
+}
+
+bool rows16(const kf_tensor4* t) {
+  if (!t || !kf::aligned16(t->ptr) || t->stride[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (t->size[i] > 1 && (t->stride[i] % 8) != 0) return false;
+  return true;
+}
+
+int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+// Mirrors kotflash_b200/_planning.py:split_kv_plan (same formula).
+extern "C" int kf_decode_num_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk,
+                                    int64_t D, int sm_count) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0 || D <= 0) return 1;
+  if (sm_count <= 0) sm_count = 148;
+  const int64_t group = Hq / Hkv > 0 ? Hq / Hkv : 1;
+  const int64_t rows_per_cta = D <= 64 ? 64 : 32;
+  const int64_t units = B * Hkv * cdiv64(group * Sq, rows_per_cta);
+  const int64_t max_by_len = cdiv64(Sk, 256) > 1 ? cdiv64(Sk, 256) : 1;
+  int64_t splits = cdiv64(2 * (int64_t)sm_count, units);
+  if (splits > max_by_len) splits = max_by_len;
+  if (splits > 512) splits = 512;
+  if (splits < 1) splits = 1;
+  const int64_t chunk = cdiv64(cdiv64(Sk, splits), 64) * 64;
+  return (int)cdiv64(Sk, chunk);
+}
+
+extern "C" size_t kf_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D,
+                                            int num_splits) {
+  if (num_splits <= 1) return 0;
+  return (size_t)num_splits * (size_t)(B * Hq * Sq) * (size_t)(D + 1) * sizeof(float) + 256;
+}
+
+extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                         const kf_tensor4* new_k, const kf_tensor4* new_v, int64_t past_len,
+                         const kf_tensor4* o, float* lse, int dtype, float scale, int num_splits,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  using kf::set_error;
+  if (!q || !k || !v || !o) return set_error(KF_ERR_INVALID, "kf_decode: null tensor descriptor");
+  if (dtype != KF_F16 && dtype != KF_BF16)
+    return set_error(KF_ERR_INVALID, "kf_decode: dtype must be fp16 or bf16");
+  const int64_t B = q->size[0], Hq = q->size[1], Sq = q->size[2], D = q->size[3];
+  const int64_t Hkv = k->size[1], Sk = k->size[2];
+  for (int i = 0; i < 4; ++i)
+    if (k->size[i] != v->size[i]) return set_error(KF_ERR_INVALID, "kf_decode: K and V shapes must match");
+  if (k->size[0] != B || k->size[3] != D)
+    return set_error(KF_ERR_INVALID, "kf_decode: K/V batch and head_dim must match Q");
+  for (int i = 0; i < 4; ++i)
+    if (o->size[i] != q->size[i]) return set_error(KF_ERR_INVALID, "kf_decode: O must have Q's shape");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0)
+    return set_error(KF_ERR_INVALID, "kf_decode: dimensions must be non-zero");
+  if (Hq % Hkv != 0)
+    return set_error(KF_ERR_INVALID, "kf_decode: num_query_heads must be divisible by num_kv_heads");
+  if (Sq > 16) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: Sq must be <= 16");
+  if (D < 16 || D > 128 || D % 8 != 0)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_decode: head_dim must be a multiple of 8 in [16, 128]");
+  if (Sk > (int64_t)1 << 30) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: Sk too large");
+  if (!rows16(q) || !rows16(k) || !rows16(v) || !rows16(o))
+    return set_error(KF_ERR_INVALID,
+                     "kf_decode: tensors need a contiguous last dim and 16-byte aligned rows");
+  const bool fused = new_k != nullptr || new_v != nullptr;
+  if (fused) {
+    if (!new_k || !new_v) return set_error(KF_ERR_INVALID, "kf_decode: new_k and new_v go together");
+    if (new_k->size[0] != B || new_k->size[1] != Hkv || new_k->size[2] != 1 || new_k->size[3] != D)
+      return set_error(KF_ERR_INVALID, "kf_decode: new K/V must be [B, Hkv, 1, D]");
+    for (int i = 0; i < 4; ++i)
+      if (new_v->size[i] != new_k->size[i])
+        return set_error(KF_ERR_INVALID, "kf_decode: new K and V shapes must match");
+    if (!rows16(new_k) || !rows16(new_v))
+      return set_error(KF_ERR_INVALID, "kf_decode: new K/V rows must be 16-byte aligned");
+    if (past_len != Sk - 1)
+      return set_error(KF_ERR_INVALID, "kf_decode: fused append needs past_len == Sk - 1");
+  }
+  if (num_splits <= 0)
+    num_splits = kf_decode_num_splits(B, Hq, Hkv, Sq, Sk, D, kf::sm_count_current_device());
+  if (num_splits > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many splits");
+  const int64_t chunk = cdiv64(cdiv64(Sk, num_splits), 64) * 64;
+  num_splits = (int)cdiv64(Sk, chunk);
+
+  DecodeArgs a;
+  a.q = static_cast<const uint16_t*>(q->ptr);
+  a.k = static_cast<const uint16_t*>(k->ptr);
+  a.v = static_cast<const uint16_t*>(v->ptr);
+  a.nk = fused ? static_cast<const uint16_t*>(new_k->ptr) : nullptr;
+  a.nv = fused ? static_cast<const uint16_t*>(new_v->ptr) : nullptr;
+  a.kw = static_cast<uint16_t*>(k->ptr);
+  a.vw = static_cast<uint16_t*>(v->ptr);
+  a.o = static_cast<uint16_t*>(o->ptr);
+  a.lse = lse;
+  for (int i = 0; i < 4; ++i) {
+    a.qs[i] = q->stride[i];
+    a.ks[i] = k->stride[i];
+    a.vs[i] = v->stride[i];
+    a.os[i] = o->stride[i];
+    a.nks[i] = fused ? new_k->stride[i] : 0;
+    a.nvs[i] = fused ? new_v->stride[i] : 0;
+  }
+  a.B = (int)B;
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.G = (int)(Hq / Hkv);
+  a.Sq = (int)Sq;
+  a.Sk = (int)Sk;
+  a.D = (int)D;
+  a.past_len = past_len;
+  a.num_splits = num_splits;
+  a.chunk = (int)chunk;
+  a.rows = a.G * a.Sq;
+  a.prow_total = B * Hq * Sq;
+  a.scale_log2 = scale * kLog2e;
+  a.part_o = nullptr;
+  a.part_lse = nullptr;
+  if (num_splits > 1) {
+    const size_t need = kf_decode_workspace_bytes(B, Hq, Sq, D, num_splits);
+    if (!workspace || workspace_bytes < need)
+      return set_error(KF_ERR_WORKSPACE, "kf_decode: workspace needs %zu bytes", need);
+    uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255);
+    a.part_o = reinterpret_cast<float*>(base);
+    a.part_lse = a.part_o + (size_t)num_splits * a.prow_total * D;
+  }
+  if (a.G * a.Sq > (1 << 20)) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many rows per KV head");
+  if ((int64_t)B * Hkv > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: B*Hkv too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = dtype == KF_BF16 ? dispatch_split<true>(a, st) : dispatch_split<false>(a, st);
+  if (rc != KF_OK || num_splits == 1) return rc;
+  MergeArgs m;
+  m.part_o = a.part_o;
+  m.part_lse = a.part_lse;
+  m.S = num_splits;
+  m.rows = a.prow_total;
+  m.D = a.D;
+  m.o = a.o;
+  m.lse = lse;
+  m.Hq = a.Hq;
+  m.Sq = a.Sq;
+  m.os0 = a.os[0];
+  m.os1 = a.os[1];
+  m.os2 = a.os[2];
+  return dtype == KF_BF16 ? launch_merge<true>(m, st) : launch_merge<false>(m, st);
+}
+
+extern "C" int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits,
+                                 int64_t rows, int64_t D, void* o, float* lse, int dtype,
+                                 void* stream) {
+  using kf::set_error;
+  if (!part_o || !part_lse || !o) return set_error(KF_ERR_INVALID, "kf_merge_partials: null pointer");
+  if (num_splits <= 0 || rows <= 0 || D <= 0 || D > 128 || D % 4 != 0)
+    return set_error(KF_ERR_INVALID, "kf_merge_partials: need splits > 0, rows > 0, D % 4 == 0, D <= 128");
+  if (dtype != KF_F16 && dtype != KF_BF16)
+    return set_error(KF_ERR_INVALID, "kf_merge_partials: dtype must be fp16 or bf16");
+  if ((reinterpret_cast<uintptr_t>(part_o) & 15) || (reinterpret_cast<uintptr_t>(o) & 7))
+    return set_error(KF_ERR_INVALID, "kf_merge_partials: misaligned buffers");
+  MergeArgs m;
+  m.part_o = part_o;
+  m.part_lse = part_lse;
+  m.S = num_splits;
+  m.rows = rows;
+  m.D = (int)D;
+  m.o = static_cast<uint16_t*>(o);
+  m.lse = lse;
+  m.Hq = 1;
+  m.Sq = 1;
+  m.os0 = D;
+  m.os1 = 0;
+  m.os2 = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == KF_BF16 ? launch_merge<true>(m, st) : launch_merge<false>(m, st);
+}

@@ -1,0 +1,432 @@
+// K1: attention forward on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces `_attention_fwd_kernel` (kotflash/kernels/triton_forward.py:21-165)
+// and its launcher `attention_forward` (triton_forward.py:372-456).  Computes
+// O = softmax(scale * Q K^T + mask) V and the row LSE (natural log) for
+// upper-left causal or full masks, GQA/MQA head mapping, fp16/bf16,
+// 16 <= D <= 128 (D % 8 == 0; columns past D are zero-filled by TMA).
+//
+// CTA = two 128-row Q tiles that share one KV head (two heads of the same
+// GQA group at the same rows, or two consecutive row blocks of one head),
+// so every K/V tile fetched by TMA feeds both.  Warp roles:
+//   warps 0-3  softmax for tile 0   (thread t owns query row t = TMEM lane t)
+//   warps 4-7  softmax for tile 1
+//   warp  8    TMA producer (Q once, then K/V blocks of 128 keys)
+//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+// Tensor memory (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// P (16-bit) overwrites the first 64 columns of its S tile and feeds the
+// PV product directly from TMEM (A operand in tensor memory).
+// The MMA issue order per KV block j is
+//   O0 += P0_j V_j ; S0 = Q0 K_{j+1}^T ; O1 += P1_j V_j ; S1 = Q1 K_{j+1}^T
+// so one tile's softmax overlaps the other tile's two GEMMs.  A tile's
+// "S ready" commit also covers its previous PV, which makes O safe to rescale
+// when the softmax sees the next S.  The running max is only raised (and O
+// rescaled) when it grows by more than 2^8, so most blocks skip the O
+// round trip; P stays <= 256, which fp16/bf16 hold exactly enough.
+#include <math.h>
+
+#include "kf_host.h"
+#include "kf_sm100.cuh"
+
+namespace {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockN = 128;
+constexpr int kThreads = 320;
+constexpr int kStages = 2;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FwdParams {
+  uint16_t* o;
+  float* lse;
+  int64_t os[4];
+  int B, Hq, Hkv, G, Sq, Sk, D;
+  int causal;
+  int m_blocks;        // cdiv(Sq, 128)
+  int slots_per_kvh;   // G * m_blocks
+  int ctas_per_kvh;    // cdiv(slots_per_kvh, 2)
+  float scale_log2;
+  int32_t* status;
+};
+
+struct __align__(8) FwdBarriers {
+  uint64_t q_full;
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_final;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, FwdBarriers* bars,
+                                         int32_t* status) {
+  if (kf::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = kf::global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (kf::mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
+      if (*(volatile int*)&bars->abort_flag) return false;
+      if (kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
+        *(volatile int*)&bars->abort_flag = 1;
+        if (status) atomicExch(status, KF_DEV_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Work item of a CTA: KV head (b, kvh) and up to two (head, row0) tiles.
+struct TileInfo {
+  int b, kvh;
+  int head[2], row0[2];
+  int valid[2];
+  int n_blocks;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const FwdParams& p) {
+  TileInfo ti;
+  const int per_bh = p.ctas_per_kvh;
+  const int bh = blockIdx.x / per_bh;
+  // heavier (later) row blocks first so causal tails do not straggle
+  const int c = per_bh - 1 - (blockIdx.x % per_bh);
+  ti.b = bh / p.Hkv;
+  ti.kvh = bh % p.Hkv;
+  int row_end_max = 0;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int slot = 2 * c + t;
+    ti.valid[t] = slot < p.slots_per_kvh;
+    const int s = ti.valid[t] ? slot : 2 * c;
+    const int mb = s / p.G, g = s % p.G;
+    ti.head[t] = ti.kvh * p.G + g;
+    ti.row0[t] = mb * kBlockM;
+    if (ti.valid[t]) row_end_max = max(row_end_max, min(ti.row0[t] + kBlockM, p.Sq));
+  }
+  const int key_end = p.causal ? min(p.Sk, row_end_max) : p.Sk;
+  ti.n_blocks = (key_end + kBlockN - 1) / kBlockN;
+  return ti;
+}
+
+template <bool BF16, int NP>
+__global__ void __launch_bounds__(kThreads, 1)
+fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+           const __grid_constant__ CUtensorMap map_v, const FwdParams p) {
+  constexpr int PANEL = kBlockM * 128;      // bytes of one 64-column panel of 128 rows
+  constexpr int TILE = NP * PANEL;          // one 128-row tile, all panels
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;                          // [2][NP][128][64]
+  uint8_t* sK = sQ + 2 * TILE;                 // [kStages][NP][128][64]
+  uint8_t* sV = sK + kStages * TILE;           // [kStages][NP][128][64]
+  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(sV + kStages * TILE);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const TileInfo ti = tile_info(p);
+  const int nblk = ti.n_blocks;
+  const int d_pad16 = (p.D + 15) & ~15;
+  const int k_steps = d_pad16 / 16;
+
+  if (tid == 0) {
+    kf::mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      kf::mbar_init(&bars->k_full[s], 1);
+      kf::mbar_init(&bars->k_empty[s], 1);
+      kf::mbar_init(&bars->v_full[s], 1);
+      kf::mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      kf::mbar_init(&bars->s_full[t], 1);
+      kf::mbar_init(&bars->p_full[t], 128);
+    }
+    kf::mbar_init(&bars->o_final, 1);
+    bars->abort_flag = 0;
+    kf::fence_barrier_init();
+  }
+  if (warp == 9) {
+    kf::tmem_alloc(&bars->tmem_base, 512);
+    kf::tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    kf::tma_prefetch_desc(&map_q);
+    kf::tma_prefetch_desc(&map_k);
+    kf::tma_prefetch_desc(&map_v);
+  }
+  kf::tc_fence_before();
+  __syncthreads();
+  kf::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int nq = ti.valid[1] ? 2 : 1;
+      kf::mbar_arrive_expect_tx(&bars->q_full, nq * TILE);
+      for (int t = 0; t < nq; ++t)
+        for (int pn = 0; pn < NP; ++pn)
+          kf::tma_load_4d(sQ + t * TILE + pn * PANEL, &map_q, &bars->q_full, pn * 64, ti.row0[t],
+                          ti.head[t], ti.b);
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = ((j / kStages) & 1) ^ 1;
+        if (!wait_bar(&bars->k_empty[s], ph, bars, p.status)) break;
+        kf::mbar_arrive_expect_tx(&bars->k_full[s], TILE);
+        for (int pn = 0; pn < NP; ++pn)
+          kf::tma_load_4d(sK + s * TILE + pn * PANEL, &map_k, &bars->k_full[s], pn * 64,
+                          j * kBlockN, ti.kvh, ti.b);
+        if (!wait_bar(&bars->v_empty[s], ph, bars, p.status)) break;
+        kf::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
+        for (int pn = 0; pn < NP; ++pn)
+          kf::tma_load_4d(sV + s * TILE + pn * PANEL, &map_v, &bars->v_full[s], pn * 64,
+                          j * kBlockN, ti.kvh, ti.b);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = kf::make_idesc_f16(BF16, kBlockM, kBlockN, 0, 0);
+      const uint32_t idesc_pv = kf::make_idesc_f16(BF16, kBlockM, d_pad16, 0, 1);
+      const uint32_t sq_u = kf::smem_u32(sQ), sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
+      const int nt = ti.valid[1] ? 2 : 1;
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t qb = sq_u + t * TILE, kb = sk_u + (j % kStages) * TILE;
+        for (int kk = 0; kk < k_steps; ++kk) {
+          const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
+          kf::umma_ss(tmem + t * 128, kf::make_sdesc(qb + off, 16, 1024),
+                      kf::make_sdesc(kb + off, 16, 1024), idesc_qk, kk > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = sv_u + (j % kStages) * TILE;
+        for (int kk = 0; kk < kBlockN / 16; ++kk) {
+          kf::umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                      kf::make_sdesc(vb + kk * 2048, PANEL, 1024), idesc_pv, (j > 0 || kk > 0));
+        }
+      };
+      bool ok = wait_bar(&bars->q_full, 0, bars, p.status) &&
+                wait_bar(&bars->k_full[0], 0, bars, p.status);
+      if (ok) {
+        kf::tc_fence_after();
+        for (int t = 0; t < nt; ++t) {
+          issue_qk(t, 0);
+          kf::umma_commit(&bars->s_full[t]);
+        }
+        kf::umma_commit(&bars->k_empty[0]);
+      }
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const bool more = j + 1 < nblk;
+        const int s1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
+        if (!(ok = wait_bar(&bars->v_full[s], ph, bars, p.status))) break;
+        if (more && !(ok = wait_bar(&bars->k_full[s1], ph1, bars, p.status))) break;
+        for (int t = 0; t < nt; ++t) {
+          if (!(ok = wait_bar(&bars->p_full[t], j & 1, bars, p.status))) break;
+          kf::tc_fence_after();
+          issue_pv(t, j);
+          if (more) {
+            issue_qk(t, j + 1);
+            kf::umma_commit(&bars->s_full[t]);
+          }
+        }
+        if (!ok) break;
+        kf::umma_commit(&bars->v_empty[s]);
+        if (more) kf::umma_commit(&bars->k_empty[s1]);
+      }
+      kf::umma_commit(&bars->o_final);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = warp >> 2;        // tile handled by this warpgroup
+    const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t s_col = t * 128, o_col = 256 + t * 128;
+    const int row = ti.row0[t] + r;
+    float m_ref = -INFINITY, l_sum = 0.f;
+    bool ok = ti.valid[t] != 0;
+    for (int j = 0; ok && j < nblk; ++j) {
+      if (!(ok = wait_bar(&bars->s_full[t], j & 1, bars, p.status))) break;
+      kf::tc_fence_after();
+      uint32_t sr[128];
+      kf::tmem_ld32(lane_base + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      kf::tmem_ld32(lane_base + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+      kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+      kf::tmem_wait_ld();
+      float x[128];
+      const int key0 = j * kBlockN;
+      const bool need_mask = (key0 + kBlockN > p.Sk) || (p.causal && key0 + kBlockN - 1 > ti.row0[t]);
+      float mx = -INFINITY;
+      if (need_mask) {
+        const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : kBlockN);
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] = c < lim ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] = __uint_as_float(sr[c]) * p.scale_log2;
+          mx = fmaxf(mx, x[c]);
+        }
+      }
+      float alpha = 1.f;
+      bool rescale_o = false;
+      if (j == 0) {
+        m_ref = mx;
+      } else if (mx > m_ref + kRescaleThreshold) {
+        alpha = kf::ex2(m_ref - mx);
+        m_ref = mx;
+        rescale_o = true;
+      }
+      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+      l_sum *= alpha;
+      uint32_t pk[64];
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = kf::ex2(x[2 * c] - m_use), p1 = kf::ex2(x[2 * c + 1] - m_use);
+        sum += p0 + p1;
+        pk[c] = kf::pack2<BF16>(p0, p1);
+      }
+      l_sum += sum;
+      kf::tmem_st32(lane_base + s_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+      kf::tmem_st32(lane_base + s_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // O row *= alpha (alpha == 1 on rows that keep their reference max)
+        for (int c0 = 0; c0 < d_pad16; c0 += 32) {
+          uint32_t orow[32];
+          kf::tmem_ld32(lane_base + o_col + c0, orow);
+          kf::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+          kf::tmem_st32(lane_base + o_col + c0, orow);
+        }
+      }
+      kf::tmem_wait_st();
+      kf::tc_fence_before();
+      kf::mbar_arrive(&bars->p_full[t]);
+    }
+    // ---------------------------------------------------------- epilogue
+    if (ok && wait_bar(&bars->o_final, 0, bars, p.status)) {
+      kf::tc_fence_after();
+      const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const bool row_ok = row < p.Sq;
+      uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)ti.head[t] * p.os[1] + (int64_t)row * p.os[2];
+      for (int c0 = 0; c0 < d_pad16; c0 += 32) {
+        uint32_t ov[32];
+        kf::tmem_ld32(lane_base + o_col + c0, ov);
+        kf::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * inv_l, __uint_as_float(ov[2 * c + 1]) * inv_l);
+        if (row_ok) {
+#pragma unroll
+          for (int g8 = 0; g8 < 4; ++g8) {
+            if (c0 + g8 * 8 < p.D)
+              *reinterpret_cast<uint4*>(orow_g + c0 + g8 * 8) =
+                  make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);
+          }
+        }
+      }
+      if (row_ok)
+        p.lse[((int64_t)ti.b * p.Hq + ti.head[t]) * p.Sq + row] =
+            l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;
+    }
+  }
+
+  kf::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    kf::tc_fence_after();
+    kf::tmem_dealloc(tmem, 512);
+  }
+}
+
+bool rows16(const kf_tensor4* t) {
+  if (!t || !kf::aligned16(t->ptr) || t->stride[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (t->size[i] > 1 && (t->stride[i] % 8) != 0) return false;
+  return true;
+}
+
+template <bool BF16, int NP>
+int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+               const FwdParams& p, cudaStream_t st) {
+  constexpr int TILE = NP * kBlockM * 128;
+  const size_t smem = 1024 + (size_t)(2 + 2 * kStages) * TILE + sizeof(FwdBarriers);
+  auto kern = fwd_kernel<BF16, NP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: cannot reserve %zu bytes of shared memory", smem);
+  const int64_t grid = (int64_t)p.B * p.Hkv * p.ctas_per_kvh;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, p);
+  return kf::check_launch("kf_attn_fwd");
+}
+
+}  // namespace
+
+extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                           const kf_tensor4* o, float* lse, int dtype, float scale, int causal,
+                           int32_t* status, void* stream) {
+  using kf::set_error;
+  if (!q || !k || !v || !o || !lse) return set_error(KF_ERR_INVALID, "kf_attn_fwd: null argument");
+  if (dtype != KF_F16 && dtype != KF_BF16)
+    return set_error(KF_ERR_INVALID, "kf_attn_fwd: dtype must be fp16 or bf16");
+  const int64_t B = q->size[0], Hq = q->size[1], Sq = q->size[2], D = q->size[3];
+  const int64_t Hkv = k->size[1], Sk = k->size[2];
+  for (int i = 0; i < 4; ++i) {
+    if (k->size[i] != v->size[i]) return set_error(KF_ERR_INVALID, "kf_attn_fwd: K and V shapes must match");
+    if (o->size[i] != q->size[i]) return set_error(KF_ERR_INVALID, "kf_attn_fwd: O must have Q's shape");
+  }
+  if (k->size[0] != B || k->size[3] != D)
+    return set_error(KF_ERR_INVALID, "kf_attn_fwd: K/V batch and head_dim must match Q");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0)
+    return set_error(KF_ERR_INVALID, "kf_attn_fwd: dimensions must be non-zero");
+  if (Hq % Hkv) return set_error(KF_ERR_INVALID, "kf_attn_fwd: Hq must be divisible by Hkv");
+  if (D < 16 || D > 128 || D % 8)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_attn_fwd: head_dim must be a multiple of 8 in [16, 128]");
+  if (Sq > (1 << 30) || Sk > (1 << 30) || B > 65535 || Hq > 65535)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_attn_fwd: problem too large");
+  if (!rows16(q) || !rows16(k) || !rows16(v) || !rows16(o))
+    return set_error(KF_ERR_INVALID, "kf_attn_fwd: tensors need a contiguous last dim and 16-byte aligned rows");
+
+  const int box_inner = 64;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = kf::encode_tmap_4d(&mq, q, box_inner, kBlockM))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mk, k, box_inner, kBlockN))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mv, v, box_inner, kBlockN))) return rc;
+
+  FwdParams p;
+  p.o = static_cast<uint16_t*>(o->ptr);
+  p.lse = lse;
+  for (int i = 0; i < 4; ++i) p.os[i] = o->stride[i];
+  p.B = (int)B;
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.G = (int)(Hq / Hkv);
+  p.Sq = (int)Sq;
+  p.Sk = (int)Sk;
+  p.D = (int)D;
+  p.causal = causal ? 1 : 0;
+  p.m_blocks = (int)((Sq + kBlockM - 1) / kBlockM);
+  p.slots_per_kvh = p.G * p.m_blocks;
+  p.ctas_per_kvh = (p.slots_per_kvh + 1) / 2;
+  p.scale_log2 = scale * kLog2e;
+  p.status = status;
+  if ((int64_t)p.B * p.Hkv * p.ctas_per_kvh > 0x7fffffffLL)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_attn_fwd: grid too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool two_panels = D > 64;
+  if (dtype == KF_BF16)
+    return two_panels ? launch_fwd<true, 2>(mq, mk, mv, p, st) : launch_fwd<true, 1>(mq, mk, mv, p, st);
+  return two_panels ? launch_fwd<false, 2>(mq, mk, mv, p, st) : launch_fwd<false, 1>(mq, mk, mv, p, st);
+}

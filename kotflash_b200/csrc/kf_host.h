@@ -1,0 +1,30 @@
+// Host-side helpers shared by the C-ABI translation units: thread-local error
+// text, argument checks, and TMA tensor-map encoding through the driver entry
+// point (so the library needs no link-time dependency on libcuda).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/kotflash_b200.h"
+
+namespace kf {
+
+int set_error(int code, const char* fmt, ...);
+
+// Returns KF_ERR_CUDA (and records the message) if the last launch failed.
+int check_launch(const char* what);
+
+// Encode a 4-D tiled TMA descriptor over a 16-bit [n0,n1,n2,n3] view whose
+// innermost dimension (n3) is contiguous.  The box is (box_inner along n3,
+// box_rows along n2, 1, 1) with 128-byte swizzle; out-of-range elements read
+// as zero.  Returns KF_OK or an error code with the message recorded.
+int encode_tmap_4d(CUtensorMap* map, const kf_tensor4* t, int box_inner, int box_rows);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count_current_device();
+
+}  // namespace kf
