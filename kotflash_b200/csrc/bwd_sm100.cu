@@ -1,13 +1,559 @@
-// K2: attention backward (placeholder until the tcgen05 kernel lands).
-#include "kf_host.h"
+// K2: attention backward on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces `attention_backward` (kotflash/kernels/triton_backward.py:335-421)
+// and its kernels `_attention_bwd_dq` (:18-91), `_attention_bwd_dkv` (:95-195),
+// `_attention_bwd_dkv_split` (:199-312) and `_attention_bwd_dkv_reduce`
+// (:315-332).  Same math as the reference's blockwise backward
+// (kotflash/attention.py:138-201): P = exp(scale*QK^T - LSE),
+// dP = dO V^T, Delta = rowsum(O*dO), dS = P (dP - Delta), dQ = scale dS K,
+// dK = scale dS^T Q, dV = P^T dO, dK/dV summed over the GQA group.
+//
+// Three launches:
+//   1. prep   : Delta and LSE*log2(e) per query row (rows padded to 64; padded
+//               rows get LSE = +inf so their P is exactly 0); dQ workspace zeroed.
+//   2. main   : one CTA per (batch, KV head, 128-key block).  K and V stay in
+//               shared memory; the CTA walks every query head of the group and
+//               every 64-row query block that can see its keys.  Per step:
+//                 S^T  = K Q^T      (SS MMA, M=128 keys, N=64 rows)
+//                 dP^T = V dO^T     (SS MMA)
+//                 softmax warps (thread = key): P^T, dS^T -> TMEM (16-bit) and
+//                 dS^T -> shared memory (128-byte swizzled, q contiguous)
+//                 dV  += P^T dO     (TS MMA, A = P^T in TMEM)
+//                 dK  += dS^T Q     (TS MMA, A = dS^T in TMEM)
+//                 dQ^T = K^T dS^T   (SS MMA, both operands MN-major)
+//               dQ^T (thread = head-dim lane) is added into an fp32 workspace
+//               with vector atomics by a dedicated warpgroup, double-buffered
+//               in TMEM.  dK/dV accumulate in TMEM for the whole group and are
+//               written once, so no dK/dV partial buffers exist.
+//   3. finish : dQ = scale * workspace, cast to the input dtype.
+// Tensor memory (512 columns): dV [0,128) dK [128,256) S^T [256,320)
+// dP^T [320,384) dQ^T buffers [384,448) [448,512).
+#include <math.h>
 
-extern "C" size_t kf_attn_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D) {
-  return (size_t)(B * Hq * Sq) * (size_t)(D + 1) * sizeof(float) + 256;
+#include "kf_host.h"
+#include "kf_sm100.cuh"
+
+namespace {
+
+constexpr int kBM = 64;    // query rows per step
+constexpr int kBN = 128;   // keys per CTA
+constexpr int kStages = 2;
+constexpr int kThreads = 320;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct BwdParams {
+  uint16_t* dk;
+  uint16_t* dv;
+  int64_t dks[4], dvs[4];
+  float* dq_acc;          // [B*Hq][nqb][D][64]
+  const float* lse2;      // [B*Hq][Sq_pad] LSE * log2(e); +inf on padded rows
+  const float* delta;     // [B*Hq][Sq_pad]
+  int B, Hq, Hkv, G, Sq, Sk, D, Sq_pad, nqb, nkb;
+  int causal;
+  float scale_log2, scale;
+  int32_t* status;
+};
+
+struct __align__(8) BwdBarriers {
+  uint64_t kv_full;
+  uint64_t qdo_full[kStages], qdo_empty[kStages];
+  uint64_t s_full, ds_full;
+  uint64_t dq_full[2], dq_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, BwdBarriers* bars,
+                                         int32_t* status) {
+  if (kf::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = kf::global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (kf::mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
+      if (*(volatile int*)&bars->abort_flag) return false;
+      if (kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
+        *(volatile int*)&bars->abort_flag = 1;
+        if (status) atomicExch(status, KF_DEV_TIMEOUT);
+        return false;
+      }
+    }
+  }
 }
 
-extern "C" int kf_attn_bwd(const kf_tensor4*, const kf_tensor4*, const kf_tensor4*,
-                           const kf_tensor4*, const float*, const kf_tensor4*,
-                           const kf_tensor4*, const kf_tensor4*, const kf_tensor4*, int, float,
-                           int, void*, size_t, int32_t*, void*) {
-  return kf::set_error(KF_ERR_UNSUPPORTED, "kf_attn_bwd: not built yet");
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          kf::smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(kf::smem_u32(bar))
+      : "memory");
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+           const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
+           const BwdParams p) {
+  constexpr int KPANEL = kBN * 128;  // 16 KB: 128 rows x 64 columns
+  constexpr int QPANEL = kBM * 128;  // 8 KB: 64 rows x 64 columns
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sK = smem;                               // 2 panels
+  uint8_t* sV = sK + 2 * KPANEL;                    // 2 panels
+  uint8_t* sQ = sV + 2 * KPANEL;                    // [stage][2 panels]
+  uint8_t* sdO = sQ + kStages * 2 * QPANEL;         // [stage][2 panels]
+  uint8_t* sdS = sdO + kStages * 2 * QPANEL;        // 128 rows x 128 B
+  float* sLD = reinterpret_cast<float*>(sdS + KPANEL);  // [stage][lse2 64 | delta 64]
+  BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(sLD + kStages * 2 * kBM);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bkv = blockIdx.x % (p.B * p.Hkv);
+  const int n = blockIdx.x / (p.B * p.Hkv);   // key block: all n = 0 CTAs launch first
+  const int b = bkv / p.Hkv, kvh = bkv % p.Hkv;
+  const int i0 = p.causal ? min((n * kBN) / kBM, p.nqb) : 0;
+  const int nq_steps = p.nqb - i0;
+  const int nsteps = p.G * nq_steps;
+  const int d_pad16 = (p.D + 15) & ~15;
+  const int k_steps = d_pad16 / 16;
+
+  if (tid == 0) {
+    kf::mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      kf::mbar_init(&bars->qdo_full[s], 1);
+      kf::mbar_init(&bars->qdo_empty[s], 1);
+    }
+    kf::mbar_init(&bars->s_full, 1);
+    kf::mbar_init(&bars->ds_full, 128);
+    for (int s = 0; s < 2; ++s) {
+      kf::mbar_init(&bars->dq_full[s], 1);
+      kf::mbar_init(&bars->dq_empty[s], 128);
+    }
+    kf::mbar_init(&bars->mma_done, 1);
+    bars->abort_flag = 0;
+    kf::fence_barrier_init();
+  }
+  if (warp == 9) {
+    kf::tmem_alloc(&bars->tmem_base, 512);
+    kf::tmem_relinquish();
+  }
+  kf::tc_fence_before();
+  __syncthreads();
+  kf::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  auto step_coords = [&](int s, int& h, int& i) {
+    h = kvh * p.G + s / nq_steps;
+    i = i0 + s % nq_steps;
+  };
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nsteps > 0) {
+      kf::mbar_arrive_expect_tx(&bars->kv_full, 4 * KPANEL);
+      for (int pn = 0; pn < 2; ++pn) {
+        kf::tma_load_4d(sK + pn * KPANEL, &map_k, &bars->kv_full, pn * 64, n * kBN, kvh, b);
+        kf::tma_load_4d(sV + pn * KPANEL, &map_v, &bars->kv_full, pn * 64, n * kBN, kvh, b);
+      }
+      for (int s = 0; s < nsteps; ++s) {
+        const int st = s % kStages;
+        if (!wait_bar(&bars->qdo_empty[st], ((s / kStages) & 1) ^ 1, bars, p.status)) break;
+        int h, i;
+        step_coords(s, h, i);
+        kf::mbar_arrive_expect_tx(&bars->qdo_full[st], 4 * QPANEL + 2 * kBM * 4);
+        for (int pn = 0; pn < 2; ++pn) {
+          kf::tma_load_4d(sQ + (st * 2 + pn) * QPANEL, &map_q, &bars->qdo_full[st], pn * 64, i * kBM, h, b);
+          kf::tma_load_4d(sdO + (st * 2 + pn) * QPANEL, &map_do, &bars->qdo_full[st], pn * 64, i * kBM, h, b);
+        }
+        const int64_t row_off = ((int64_t)b * p.Hq + h) * p.Sq_pad + (int64_t)i * kBM;
+        bulk_load(sLD + st * 2 * kBM, p.lse2 + row_off, kBM * 4, &bars->qdo_full[st]);
+        bulk_load(sLD + st * 2 * kBM + kBM, p.delta + row_off, kBM * 4, &bars->qdo_full[st]);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nsteps > 0) {
+      const uint32_t idesc_s = kf::make_idesc_f16(BF16, 128, kBM, 0, 0);
+      const uint32_t idesc_kv = kf::make_idesc_f16(BF16, 128, d_pad16, 0, 1);
+      const uint32_t idesc_q = kf::make_idesc_f16(BF16, 128, kBM, 1, 1);
+      const uint32_t sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
+      const uint32_t sq_u = kf::smem_u32(sQ), sdo_u = kf::smem_u32(sdO), sds_u = kf::smem_u32(sdS);
+      bool ok = wait_bar(&bars->kv_full, 0, bars, p.status);
+      for (int s = 0; ok && s < nsteps; ++s) {
+        const int st = s % kStages;
+        if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        const uint32_t qb = sq_u + st * 2 * QPANEL, dob = sdo_u + st * 2 * QPANEL;
+        for (int kk = 0; kk < k_steps; ++kk) {
+          const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
+          const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
+          kf::umma_ss(tmem + 256, kf::make_sdesc(sk_u + ka, 16, 1024),
+                      kf::make_sdesc(qb + qa, 16, 1024), idesc_s, kk > 0);
+          kf::umma_ss(tmem + 320, kf::make_sdesc(sv_u + ka, 16, 1024),
+                      kf::make_sdesc(dob + qa, 16, 1024), idesc_s, kk > 0);
+        }
+        kf::umma_commit(&bars->s_full);
+        if (!(ok = wait_bar(&bars->ds_full, s & 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        for (int kk = 0; kk < kBM / 16; ++kk) {
+          const uint32_t acc = (s > 0 || kk > 0);
+          kf::umma_ts(tmem + 0, tmem + 256 + kk * 8, kf::make_sdesc(dob + kk * 2048, QPANEL, 1024),
+                      idesc_kv, acc);
+          kf::umma_ts(tmem + 128, tmem + 320 + kk * 8, kf::make_sdesc(qb + kk * 2048, QPANEL, 1024),
+                      idesc_kv, acc);
+        }
+        const int buf = s & 1;
+        if (!(ok = wait_bar(&bars->dq_empty[buf], ((s >> 1) & 1) ^ 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          kf::umma_ss(tmem + 384 + buf * 64, kf::make_sdesc(sk_u + kk * 2048, KPANEL, 1024),
+                      kf::make_sdesc(sds_u + kk * 2048, KPANEL, 1024), idesc_q, kk > 0);
+        }
+        kf::umma_commit(&bars->dq_full[buf]);
+        kf::umma_commit(&bars->qdo_empty[st]);
+      }
+      kf::umma_commit(&bars->mma_done);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ P / dS (thread = key)
+    const int kr = warp * 32 + lane;
+    const int key = n * kBN + kr;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    for (int s = 0; ok && s < nsteps; ++s) {
+      const int st = s % kStages;
+      if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
+      if (!(ok = wait_bar(&bars->s_full, s & 1, bars, p.status))) break;
+      kf::tc_fence_after();
+      int h, i;
+      step_coords(s, h, i);
+      uint32_t sr[64], dr[64];
+      kf::tmem_ld32(lane_base + 256, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      kf::tmem_ld32(lane_base + 288, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      kf::tmem_ld32(lane_base + 320, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      kf::tmem_ld32(lane_base + 352, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      kf::tmem_wait_ld();
+      const float* lse2 = sLD + st * 2 * kBM;
+      const float* dlt = lse2 + kBM;
+      const int q0 = i * kBM;
+      // visible iff key < Sk and (not causal or key <= q)
+      const int first_q = p.causal ? key - q0 : 0;  // columns c >= first_q are visible
+      const bool key_ok = key < p.Sk;
+      uint32_t pk[32], dk[32];
+#pragma unroll
+      for (int c = 0; c < kBM; c += 2) {
+        float pr[2], dsv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = c + e;
+          const bool vis = key_ok && cc >= first_q;
+          const float x = __uint_as_float(sr[cc]) * p.scale_log2 - lse2[cc];
+          pr[e] = vis ? kf::ex2(x) : 0.f;
+          dsv[e] = pr[e] * (__uint_as_float(dr[cc]) - dlt[cc]);
+        }
+        pk[c / 2] = kf::pack2<BF16>(pr[0], pr[1]);
+        dk[c / 2] = kf::pack2<BF16>(dsv[0], dsv[1]);
+      }
+      kf::tmem_st32(lane_base + 256, pk);
+      kf::tmem_st32(lane_base + 320, dk);
+      // dS^T row -> shared memory, 128-byte swizzle (16-byte chunk c at c ^ (row & 7))
+      uint8_t* row_ptr = sdS + kr * 128;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<uint4*>(row_ptr + ((c8 ^ (kr & 7)) << 4)) =
+            make_uint4(dk[4 * c8], dk[4 * c8 + 1], dk[4 * c8 + 2], dk[4 * c8 + 3]);
+      kf::fence_proxy_async_smem();
+      kf::tmem_wait_st();
+      kf::tc_fence_before();
+      kf::mbar_arrive(&bars->ds_full);
+    }
+  } else {
+    // ------------------------------------------------------------ dQ drain (thread = head-dim lane)
+    const int dl = (warp - 4) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+    bool ok = true;
+    for (int s = 0; ok && s < nsteps; ++s) {
+      const int buf = s & 1;
+      if (!(ok = wait_bar(&bars->dq_full[buf], (s >> 1) & 1, bars, p.status))) break;
+      kf::tc_fence_after();
+      uint32_t v[64];
+      kf::tmem_ld32(lane_base + 384 + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      kf::tmem_ld32(lane_base + 416 + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      kf::tmem_wait_ld();
+      kf::tc_fence_before();
+      kf::mbar_arrive(&bars->dq_empty[buf]);
+      if (dl < p.D) {
+        int h, i;
+        step_coords(s, h, i);
+        float4* dst = reinterpret_cast<float4*>(
+            p.dq_acc + ((((int64_t)b * p.Hq + h) * p.nqb + i) * p.D + dl) * kBM);
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          atomicAdd(dst + c, make_float4(__uint_as_float(v[4 * c]), __uint_as_float(v[4 * c + 1]),
+                                         __uint_as_float(v[4 * c + 2]), __uint_as_float(v[4 * c + 3])));
+      }
+    }
+  }
+
+  // ---------------------------------------------------------- dK / dV epilogue
+  if (warp < 8) {
+    const bool is_dk = warp >= 4;
+    const int kr = (warp & 3) * 32 + lane;
+    const int key = n * kBN + kr;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    uint16_t* dst = is_dk ? p.dk + b * p.dks[0] + (int64_t)kvh * p.dks[1] + (int64_t)key * p.dks[2]
+                          : p.dv + b * p.dvs[0] + (int64_t)kvh * p.dvs[1] + (int64_t)key * p.dvs[2];
+    const float mul = is_dk ? p.scale : 1.f;
+    const bool have = nsteps > 0 && wait_bar(&bars->mma_done, 0, bars, p.status);
+    if (have) kf::tc_fence_after();
+    if (nsteps == 0 || have) {
+      for (int c0 = 0; c0 < d_pad16; c0 += 32) {
+        uint32_t ov[32];
+        if (have) {
+          kf::tmem_ld32(lane_base + (is_dk ? 128 : 0) + c0, ov);
+          kf::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) ov[c] = 0u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * mul, __uint_as_float(ov[2 * c + 1]) * mul);
+        if (key < p.Sk) {
+#pragma unroll
+          for (int g8 = 0; g8 < 4; ++g8)
+            if (c0 + g8 * 8 < p.D)
+              *reinterpret_cast<uint4*>(dst + c0 + g8 * 8) =
+                  make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);
+        }
+      }
+    }
+  }
+
+  kf::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    kf::tc_fence_after();
+    kf::tmem_dealloc(tmem, 512);
+  }
+}
+
+// Delta = rowsum(O * dO) and LSE * log2(e), one warp per (padded) row.
+struct PrepArgs {
+  const uint16_t* o;
+  const uint16_t* dout;
+  const float* lse;
+  float* lse2;
+  float* delta;
+  int64_t os[4], dos[4];
+  int Hq, Sq, Sq_pad, D;
+  int64_t rows;  // B*Hq*Sq_pad
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= a.rows) return;
+  const int64_t bh = row / a.Sq_pad;
+  const int q = (int)(row % a.Sq_pad);
+  if (q >= a.Sq) {
+    if (lane == 0) {
+      a.lse2[row] = INFINITY;
+      a.delta[row] = 0.f;
+    }
+    return;
+  }
+  const int64_t b = bh / a.Hq, h = bh % a.Hq;
+  const uint16_t* orow = a.o + b * a.os[0] + h * a.os[1] + (int64_t)q * a.os[2];
+  const uint16_t* drow = a.dout + b * a.dos[0] + h * a.dos[1] + (int64_t)q * a.dos[2];
+  float acc = 0.f;
+  for (int d = lane * 4; d < a.D; d += 128) {
+    const uint2 ov = *reinterpret_cast<const uint2*>(orow + d);
+    const uint2 dv = *reinterpret_cast<const uint2*>(drow + d);
+    const float2 o0 = kf::unpack2<BF16>(ov.x), o1 = kf::unpack2<BF16>(ov.y);
+    const float2 d0 = kf::unpack2<BF16>(dv.x), d1 = kf::unpack2<BF16>(dv.y);
+    acc += o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    a.delta[row] = acc;
+    a.lse2[row] = a.lse[bh * a.Sq + q] * kLog2e;
+  }
+}
+
+// dQ = scale * workspace ([bh][qb][D][64] fp32) -> dq [B,Hq,Sq,D] in the input dtype.
+struct FinishArgs {
+  const float* acc;
+  uint16_t* dq;
+  int64_t qs[4];
+  int Hq, Sq, D, nqb;
+  float scale;
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) finish_kernel(const FinishArgs a) {
+  __shared__ float tile[128][kBM + 1];
+  const int qb = blockIdx.x, bh = blockIdx.y;
+  const float* src = a.acc + ((int64_t)bh * a.nqb + qb) * a.D * kBM;
+  for (int idx = threadIdx.x; idx < a.D * kBM; idx += 256) tile[idx / kBM][idx % kBM] = src[idx];
+  __syncthreads();
+  const int b = bh / a.Hq, h = bh % a.Hq;
+  const int dv = a.D / 2;
+  for (int idx = threadIdx.x; idx < kBM * dv; idx += 256) {
+    const int r = idx / dv, d2 = (idx % dv) * 2;
+    const int q = qb * kBM + r;
+    if (q >= a.Sq) continue;
+    uint16_t* dst = a.dq + b * a.qs[0] + (int64_t)h * a.qs[1] + (int64_t)q * a.qs[2] + d2;
+    *reinterpret_cast<uint32_t*>(dst) = kf::pack2<BF16>(tile[d2][r] * a.scale, tile[d2 + 1][r] * a.scale);
+  }
+}
+
+bool rows16(const kf_tensor4* t) {
+  if (!t || !kf::aligned16(t->ptr) || t->stride[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (t->size[i] > 1 && (t->stride[i] % 8) != 0) return false;
+  return true;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+template <bool BF16>
+int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const kf_tensor4* o,
+            const float* lse, const kf_tensor4* dout, const kf_tensor4* dq, const kf_tensor4* dk,
+            const kf_tensor4* dv, float scale, int causal, void* workspace, int32_t* status,
+            cudaStream_t st) {
+  const int B = (int)q->size[0], Hq = (int)q->size[1], Sq = (int)q->size[2], D = (int)q->size[3];
+  const int Hkv = (int)k->size[1], Sk = (int)k->size[2];
+  const int Sq_pad = (Sq + kBM - 1) / kBM * kBM;
+  const int nqb = Sq_pad / kBM;
+  const int nkb = (Sk + kBN - 1) / kBN;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+  float* dq_acc = reinterpret_cast<float*>(ws);
+  const size_t acc_bytes = align256((size_t)B * Hq * nqb * D * kBM * 4);
+  float* lse2 = reinterpret_cast<float*>(ws + acc_bytes);
+  const size_t row_bytes = align256((size_t)B * Hq * Sq_pad * 4);
+  float* delta = reinterpret_cast<float*>(ws + acc_bytes + row_bytes);
+
+  if (cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * nqb * D * kBM * 4, st) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: memset of the dQ workspace failed");
+
+  PrepArgs pa;
+  pa.o = static_cast<const uint16_t*>(o->ptr);
+  pa.dout = static_cast<const uint16_t*>(dout->ptr);
+  pa.lse = lse;
+  pa.lse2 = lse2;
+  pa.delta = delta;
+  for (int i = 0; i < 4; ++i) {
+    pa.os[i] = o->stride[i];
+    pa.dos[i] = dout->stride[i];
+  }
+  pa.Hq = Hq;
+  pa.Sq = Sq;
+  pa.Sq_pad = Sq_pad;
+  pa.D = D;
+  pa.rows = (int64_t)B * Hq * Sq_pad;
+  prep_kernel<BF16><<<(unsigned)((pa.rows + 7) / 8), 256, 0, st>>>(pa);
+  int rc = kf::check_launch("kf_attn_bwd prep");
+  if (rc) return rc;
+
+  CUtensorMap mq, mk, mv, mdo;
+  if ((rc = kf::encode_tmap_4d(&mq, q, 64, kBM))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mdo, dout, 64, kBM))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mk, k, 64, kBN))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mv, v, 64, kBN))) return rc;
+
+  BwdParams p;
+  p.dk = static_cast<uint16_t*>(dk->ptr);
+  p.dv = static_cast<uint16_t*>(dv->ptr);
+  for (int i = 0; i < 4; ++i) {
+    p.dks[i] = dk->stride[i];
+    p.dvs[i] = dv->stride[i];
+  }
+  p.dq_acc = dq_acc;
+  p.lse2 = lse2;
+  p.delta = delta;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = Hq / Hkv;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.D = D;
+  p.Sq_pad = Sq_pad;
+  p.nqb = nqb;
+  p.nkb = nkb;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * kLog2e;
+  p.scale = scale;
+  p.status = status;
+  const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 128 * 128 +
+                      kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
+  auto kern = bwd_kernel<BF16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
+  const int64_t grid = (int64_t)B * Hkv * nkb;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, p);
+  if ((rc = kf::check_launch("kf_attn_bwd main"))) return rc;
+
+  FinishArgs fa;
+  fa.acc = dq_acc;
+  fa.dq = static_cast<uint16_t*>(dq->ptr);
+  for (int i = 0; i < 4; ++i) fa.qs[i] = dq->stride[i];
+  fa.Hq = Hq;
+  fa.Sq = Sq;
+  fa.D = D;
+  fa.nqb = nqb;
+  fa.scale = scale;
+  finish_kernel<BF16><<<dim3(nqb, B * Hq), 256, 0, st>>>(fa);
+  return kf::check_launch("kf_attn_bwd finish");
+}
+
+}  // namespace
+
+extern "C" size_t kf_attn_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D) {
+  const int64_t Sq_pad = (Sq + kBM - 1) / kBM * kBM;
+  return 256 + align256((size_t)(B * Hq * Sq_pad) * D * 4) + 2 * align256((size_t)(B * Hq * Sq_pad) * 4);
+}
+
+extern "C" int kf_attn_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                           const kf_tensor4* o, const float* lse, const kf_tensor4* dout,
+                           const kf_tensor4* dq, const kf_tensor4* dk, const kf_tensor4* dv,
+                           int dtype, float scale, int causal, void* workspace,
+                           size_t workspace_bytes, int32_t* status, void* stream) {
+  using kf::set_error;
+  if (!q || !k || !v || !o || !lse || !dout || !dq || !dk || !dv)
+    return set_error(KF_ERR_INVALID, "kf_attn_bwd: null argument");
+  if (dtype != KF_F16 && dtype != KF_BF16)
+    return set_error(KF_ERR_INVALID, "kf_attn_bwd: dtype must be fp16 or bf16");
+  const int64_t B = q->size[0], Hq = q->size[1], Sq = q->size[2], D = q->size[3];
+  const int64_t Hkv = k->size[1], Sk = k->size[2];
+  for (int i = 0; i < 4; ++i) {
+    if (k->size[i] != v->size[i] || dk->size[i] != k->size[i] || dv->size[i] != k->size[i])
+      return set_error(KF_ERR_INVALID, "kf_attn_bwd: K, V, dK and dV shapes must match");
+    if (o->size[i] != q->size[i] || dout->size[i] != q->size[i] || dq->size[i] != q->size[i])
+      return set_error(KF_ERR_INVALID, "kf_attn_bwd: O, dO and dQ must have Q's shape");
+  }
+  if (k->size[0] != B || k->size[3] != D)
+    return set_error(KF_ERR_INVALID, "kf_attn_bwd: K/V batch and head_dim must match Q");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0 || Hq % Hkv)
+    return set_error(KF_ERR_INVALID, "kf_attn_bwd: bad dimensions or head grouping");
+  if (D < 16 || D > 128 || D % 8)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_attn_bwd: head_dim must be a multiple of 8 in [16, 128]");
+  if (Sq > (1 << 30) || Sk > (1 << 30) || B * Hq > 65535)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_attn_bwd: problem too large");
+  for (const kf_tensor4* t : {q, k, v, o, dout, dq, dk, dv})
+    if (!rows16(t))
+      return set_error(KF_ERR_INVALID, "kf_attn_bwd: tensors need a contiguous last dim and 16-byte aligned rows");
+  const size_t need = kf_attn_bwd_workspace_bytes(B, Hq, Sq, D);
+  if (!workspace || workspace_bytes < need)
+    return set_error(KF_ERR_WORKSPACE, "kf_attn_bwd: workspace needs %zu bytes", need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == KF_BF16)
+    return run_bwd<true>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, status, st);
+  return run_bwd<false>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, status, st);
 }

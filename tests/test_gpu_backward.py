@@ -1,0 +1,92 @@
+# SPDX-License-Identifier: Apache-2.0
+"""K2 tcgen05 backward (dQ, dK, dV) vs the fp32 oracle (GPU)."""
+import pytest
+import torch
+
+from kotflash_b200 import attention
+from kotflash_b200.attention import attention_backward, attention_forward
+from oracle import attention_oracle as oracle
+from tests._util import check_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand(shape, dtype, seed, scale=1.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, device="cuda", generator=g) * scale).to(dtype)
+
+
+def _run(b, hq, hkv, sq, sk, d, causal, dtype, seed=12, q_scale=1.0):
+    q = _rand((b, hq, sq, d), dtype, seed, q_scale).requires_grad_(True)
+    k = _rand((b, hkv, sk, d), dtype, seed + 1).requires_grad_(True)
+    v = _rand((b, hkv, sk, d), dtype, seed + 2).requires_grad_(True)
+    do = _rand((b, hq, sq, d), dtype, seed + 3)
+    out = attention(q, k, v, causal=causal, backend="triton")
+    dq, dk, dv = torch.autograd.grad(out, (q, k, v), do)
+    eo, _lse, edq, edk, edv = oracle.forward_backward(q.detach(), k.detach(), v.detach(), do,
+                                                       causal=causal)
+    tag = f"{b},{hq},{hkv},{sq},{sk},{d},{causal},{dtype}"
+    check_close(out, eo, name=f"bwd-path O {tag}")
+    check_close(dq, edq, name=f"dQ {tag}")
+    check_close(dk, edk, name=f"dK {tag}")
+    check_close(dv, edv, name=f"dV {tag}")
+
+
+@pytest.mark.parametrize(
+    ("hq", "hkv", "sq", "sk", "head_dim", "causal"),
+    [   # reference tests/test_triton.py:160-173
+        (4, 4, 64, 80, 32, False),
+        (8, 2, 64, 80, 64, True),
+        (8, 1, 80, 64, 32, True),
+        (8, 2, 48, 64, 72, False),
+        (4, 4, 48, 64, 96, True),
+        (8, 1, 64, 48, 128, False),
+        (8, 2, 1024, 1024, 64, True),
+        (4, 1, 1024, 768, 32, False),
+        (4, 2, 2048, 2048, 32, True),
+        (8, 2, 1, 1024, 64, False),
+    ],
+)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_backward_reference_shapes(hq, hkv, sq, sk, head_dim, causal, dtype):
+    _run(1, hq, hkv, sq, sk, head_dim, causal, dtype)
+
+
+@pytest.mark.parametrize(
+    "b,hq,hkv,sq,sk,d,causal",
+    [
+        (2, 4, 2, 200, 333, 128, True),     # Sk > Sq causal: trailing key blocks get zero grads
+        (1, 2, 2, 129, 1, 64, False),       # single key
+        (1, 4, 2, 7, 130, 16, True),
+        (2, 6, 3, 300, 300, 80, False),
+        (1, 2, 1, 77, 91, 20, True),        # head dim not a multiple of 8 (padded)
+    ],
+)
+def test_backward_edge_shapes(b, hq, hkv, sq, sk, d, causal):
+    _run(b, hq, hkv, sq, sk, d, causal, torch.bfloat16, seed=3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_backward_prefill_config_full_size(dtype):
+    """BASELINE cfg2 fwd+bwd at full size (B4 Hq32 Hkv8 S4096 D128, causal,
+    q scaled by 1/sqrt(D)); oracle run per batch on the GPU in fp32."""
+    b, hq, hkv, s, d = 4, 32, 8, 4096, 128
+    q = _rand((b, hq, s, d), dtype, 21, d ** -0.5)
+    k = _rand((b, hkv, s, d), dtype, 22)
+    v = _rand((b, hkv, s, d), dtype, 23)
+    do = _rand((b, hq, s, d), dtype, 24)
+    out, lse = attention_forward(q, k, v, causal=True, scale=d ** -0.5)
+    dq, dk, dv = attention_backward(q, k, v, out, lse, do, causal=True, scale=d ** -0.5)
+    for i in range(b):
+        sl = slice(i, i + 1)
+        eo, el, edq, edk, edv = oracle.forward_backward(q[sl], k[sl], v[sl], do[sl], causal=True)
+        check_close(dq[sl], edq, name=f"cfg2 dQ batch {i}")
+        check_close(dk[sl], edk, name=f"cfg2 dK batch {i}")
+        check_close(dv[sl], edv, name=f"cfg2 dV batch {i}")
+
+
+@pytest.mark.parametrize("d", [72, 96])
+@pytest.mark.parametrize("causal", [False, True])
+def test_backward_odd_head_dim_config(d, causal):
+    """BASELINE cfg5 geometry (B2 Hq16 Hkv4 D72/96 fp16) at S=2048 (oracle cost)."""
+    _run(2, 16, 4, 2048, 2048, d, causal, torch.float16, seed=5)
