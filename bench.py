@@ -1,0 +1,601 @@
+#!/usr/bin/env python3
+# SPDX-License-Identifier: Apache-2.0
+"""Benchmark of the KOTFlash attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (BASELINE.json metric "attn fwd+bwd TFLOP/s & %peak"): one step is
+one causal forward + backward of the GQA prefill config B=4, Hq=32, Hkv=8,
+Sq=Sk=4096, D=128, bf16, q scaled by 1/sqrt(D), through the public
+``kotflash_b200.attention`` API with autograd.  The job is sharded by
+(batch x KV-head group) units with no communication: every rank owns the
+32 units of one full config (global batch 4*N), so the scaling is weak.
+FLOPs count only visible (q, k) pairs: fwd 4*B*Hq*D*P, bwd 2.5x fwd.
+
+Also reported, in the same JSON line:
+  * ``decode``: split-KV decode sweep (B2 Hq8 Hkv2 D64 fp16, Sq 1/4/16, Sk up
+    to 131072) in us/token and HBM GB/s, timed as CUDA-graph replays over
+    rotating K/V copies (working set > 3x L2); the KV-cache loop (capacity
+    32768, B8 Hq32 Hkv8 D128 bf16, 4096-token prefill append then 256 fused
+    append+decode steps in one CUDA graph);
+  * ``decode_multi_gpu`` (N > 1): Sk=131072 split across ranks, one NCCL
+    all-gather of packed (O, LSE) partials, merge; compute and exchange
+    timed separately, max over ranks.
+  * ``cpu_baseline``: the reference's CPU route (PyTorch SDPA + autograd,
+    restated in oracle/) on one (batch, KV-head) unit on the host cores.
+
+``--impl reference`` runs only that CPU route (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG = dict(B=4, Hq=32, Hkv=8, S=4096, D=128)
+METRIC = "attn fwd+bwd TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def causal_pairs(sq: int, sk: int) -> int:
+    n = min(sq, sk)
+    return n * (n + 1) // 2 + max(0, sq - sk) * sk
+
+
+def fwd_flops(b, hq, sq, sk, d, causal=True) -> float:
+    pairs = causal_pairs(sq, sk) if causal else sq * sk
+    return 4.0 * b * hq * d * pairs
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            j = json.loads(p.read_text())
+            return {"hbm_gbs": float(j["hbm_gbs"]), "bf16_tflops": float(j["bf16_tflops"]),
+                    "bf16_tflops_sustained": float(j.get("bf16_tflops_sustained", j["bf16_tflops"])),
+                    "source": "measured"}
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        loaded = [s for s, pw in zip(sm, power) if pw > 300.0] or sm
+        return {
+            "sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# --------------------------------------------------------------------------- dist
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- prefill fwd+bwd
+def make_prefill_inputs(dtype, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    b, hq, hkv, s, d = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    q = (torch.randn(b, hq, s, d, device=device, generator=g) * d ** -0.5).to(dtype)
+    k = torch.randn(b, hkv, s, d, device=device, generator=g).to(dtype)
+    v = torch.randn(b, hkv, s, d, device=device, generator=g).to(dtype)
+    do = torch.randn(b, hq, s, d, device=device, generator=g).to(dtype)
+    return q, k, v, do
+
+
+def prefill_step(q, k, v, do, ev=None):
+    from kotflash_b200 import attention
+
+    q.requires_grad_(True)
+    k.requires_grad_(True)
+    v.requires_grad_(True)
+    if ev is not None:
+        ev[0].record()
+    out = attention(q, k, v, causal=True, backend="triton")
+    if ev is not None:
+        ev[1].record()
+    grads = torch.autograd.grad(out, (q, k, v), do)
+    if ev is not None:
+        ev[2].record()
+    return out, grads
+
+
+def bench_prefill(args, world, rank, local, dtype):
+    q, k, v, do = make_prefill_inputs(dtype, 1234 + rank, "cuda")
+    for _ in range(args.warmup):
+        prefill_step(q, k, v, do)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if not args.no_clocks else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        prefill_step(q, k, v, do, evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    total_ms = max_over_ranks(start.elapsed_time(end), world)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    return total_ms / args.steps, fwd_ms, bwd_ms, clocks
+
+
+def bench_prefill_e2e(args, world, rank, dtype):
+    """Same step with host (pinned) inputs copied in and all outputs copied out."""
+    hq_, hk_, hv_, hdo_ = (t.cpu().pin_memory() for t in make_prefill_inputs(dtype, 99 + rank, "cuda"))
+    dq_h = torch.empty_like(hq_).pin_memory()
+    dk_h = torch.empty_like(hk_).pin_memory()
+    dv_h = torch.empty_like(hv_).pin_memory()
+    o_h = torch.empty_like(hq_).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, hdo_))
+    d2h = sum(t.numel() * t.element_size() for t in (o_h, dq_h, dk_h, dv_h))
+
+    def step():
+        q = hq_.to("cuda", non_blocking=True)
+        k = hk_.to("cuda", non_blocking=True)
+        v = hv_.to("cuda", non_blocking=True)
+        do = hdo_.to("cuda", non_blocking=True)
+        out, (dq, dk, dv) = prefill_step(q, k, v, do)
+        o_h.copy_(out.detach(), non_blocking=True)
+        dq_h.copy_(dq, non_blocking=True)
+        dk_h.copy_(dk, non_blocking=True)
+        dv_h.copy_(dv, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(2, args.steps // 2)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world) / steps
+    return ms, h2d, d2h
+
+
+# --------------------------------------------------------------------------- decode
+def _graph_time(fn, reps, replays=5):
+    """Capture ``reps`` calls of fn(i) in one CUDA graph; mean ms per call over replays."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(min(reps, 3)):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(replays):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) / reps)
+    del g
+    return min(times)
+
+
+def bench_decode_sweep(peaks):
+    from kotflash_b200.attention import _decode_forward
+
+    res = []
+    for sq in (1, 4, 16):
+        for sk in (1024, 2048, 8192, 32768, 131072):
+            kv_bytes = 2 * 2 * 2 * sk * 64 * 2
+            copies = max(1, min(256, math.ceil(3 * L2_BYTES / kv_bytes)))
+            g = torch.Generator(device="cuda").manual_seed(sk + sq)
+            ks = torch.randn(copies, 2, 2, sk, 64, device="cuda", generator=g, dtype=torch.float32).half()
+            vs = torch.randn(copies, 2, 2, sk, 64, device="cuda", generator=g, dtype=torch.float32).half()
+            qs = torch.randn(copies, 2, 8, sq, 64, device="cuda", generator=g).half()
+            reps = max(copies, 8)
+            ms = _graph_time(lambda i: _decode_forward(qs[i % copies], ks[i % copies], vs[i % copies],
+                                                       scale=0.125, want_lse=False), reps)
+            alg = 1024 * sk + 4096 * sq + 64 * sq  # K+V read, Q read + O write (+LSE)
+            gbs = alg / (ms * 1e-3) / 1e9
+            res.append({"sq": sq, "sk": sk, "us_per_call": round(ms * 1e3, 2),
+                        "us_per_token": round(ms * 1e3 / sq, 3), "hbm_gbs": round(gbs, 1),
+                        "hbm_frac": round(gbs / peaks["hbm_gbs"], 3)})
+            del ks, vs, qs
+            torch.cuda.empty_cache()
+    return res
+
+
+def bench_cache_loop(peaks):
+    from kotflash_b200.cache import PreallocatedKVCache
+
+    b, hkv, hq, d, cap, pre, steps = 8, 8, 32, 128, 32768, 4096, 256
+    cache = PreallocatedKVCache(b, hkv, cap, d, device="cuda", dtype=torch.bfloat16)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    pk = torch.randn(b, hkv, pre, d, device="cuda", generator=g).bfloat16()
+    pv = torch.randn(b, hkv, pre, d, device="cuda", generator=g).bfloat16()
+    # prefill append bandwidth (K4), timed as graph replays of the same append
+    ms_app = _graph_time(lambda i: _append_at(cache, pk, pv, 0), 8)
+    app_bytes = 2 * 2 * pk.numel() * 2  # read new K,V + write cache K,V
+    cache.append(pk, pv)
+    nk = torch.randn(steps, b, hkv, 1, d, device="cuda", generator=g).bfloat16()
+    nv = torch.randn(steps, b, hkv, 1, d, device="cuda", generator=g).bfloat16()
+    qq = torch.randn(steps, b, hq, 1, d, device="cuda", generator=g).bfloat16()
+    base = cache.length
+
+    def one(i):
+        cache.length = base + (i % steps)
+        with torch.inference_mode():
+            cache.append_and_attend(qq[i % steps], nk[i % steps], nv[i % steps])
+
+    ms = _graph_time(one, steps, replays=3)
+    cache.length = base + steps
+    mean_len = base + (steps + 1) / 2
+    step_bytes = 2 * b * hkv * mean_len * d * 2 + 2 * b * hq * d * 2 + 2 * b * hkv * d * 2
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    return {
+        "prefill_append": {"tokens": pre, "us": round(ms_app * 1e3, 2),
+                           "hbm_gbs": round(app_bytes / (ms_app * 1e-3) / 1e9, 1),
+                           "hbm_frac": round(app_bytes / (ms_app * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)},
+        "steps": steps, "us_per_step": round(ms * 1e3, 2), "us_per_token": round(ms * 1e3, 2),
+        "loop_ms": round(ms * steps, 3), "hbm_gbs": round(gbs, 1),
+        "hbm_frac": round(gbs / peaks["hbm_gbs"], 3),
+        "note": "fused append+decode, 256 steps in one CUDA graph; working set 134-143 MB (> L2)",
+    }
+
+
+def _append_at(cache, k, v, start):
+    from kotflash_b200._cuda_append import append_kv_cuda
+
+    append_kv_cuda(cache.k, cache.v, k, v, start)
+
+
+def bench_decode_multi_gpu(world, rank):
+    """cfg3 at Sk=131072, KV split across ranks; compute and exchange timed apart."""
+    from kotflash_b200 import distributed as kd
+    from kotflash_b200.attention import _decode_forward
+
+    out = []
+    sk = 131072
+    for sq in (1, 16):
+        lo, hi = kd.kv_chunk(sk, world, rank)
+        g = torch.Generator(device="cuda").manual_seed(5)
+        k_full = torch.randn(2, 2, sk, 64, device="cuda", generator=g).half()
+        v_full = torch.randn(2, 2, sk, 64, device="cuda", generator=g).half()
+        q = torch.randn(2, 8, sq, 64, device="cuda", generator=g).half()
+        kl, vl = k_full[:, :, lo:hi].contiguous(), v_full[:, :, lo:hi].contiguous()
+        del k_full, v_full
+        for _ in range(5):
+            kd.decode_kv_split(q, kl, vl, scale=0.125)
+        torch.cuda.synchronize()
+        t_c, t_x, t_all = [], [], []
+        for _ in range(20):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            barrier(world)
+            e[0].record()
+            o, lse = _decode_forward(q, kl, vl, scale=0.125, want_lse=True)
+            e[1].record()
+            po, pl = kd.gather_partials(kd.pack_partial(o, lse))
+            e[2].record()
+            kd.merge_partials(po, pl, tuple(q.shape), q.dtype)
+            e[3].record()
+            torch.cuda.synchronize()
+            t_c.append(e[0].elapsed_time(e[1]))
+            t_x.append(e[1].elapsed_time(e[2]))
+            t_all.append(e[0].elapsed_time(e[3]))
+        c = max_over_ranks(statistics.median(t_c), world)
+        x = max_over_ranks(statistics.median(t_x), world)
+        a = max_over_ranks(statistics.median(t_all), world)
+        out.append({"sq": sq, "sk": sk, "ranks": world, "compute_us": round(c * 1e3, 2),
+                    "allgather_us": round(x * 1e3, 2), "total_us": round(a * 1e3, 2),
+                    "us_per_token": round(a * 1e3 / sq, 3)})
+    return out
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_unit_sample(dtype_name: str, budget_s: float = 12.0, min_runs: int = 1):
+    """Time the reference CPU route on (batch, KV-head) units of the prefill config.
+
+    One unit = one KV head with its Hq/Hkv query heads at S=4096, D=128,
+    causal.  Runs units until ``budget_s`` of CPU time is spent; returns
+    (TFLOP/s, seconds per unit, dtype used, units run, threads)."""
+    from oracle import attention_oracle as oracle
+
+    g = torch.Generator().manual_seed(0)
+    group = CFG["Hq"] // CFG["Hkv"]
+    s, d = CFG["S"], CFG["D"]
+    dt = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    try:
+        q = (torch.randn(1, group, s, d, generator=g) * d ** -0.5).to(dt)
+        k = torch.randn(1, 1, s, d, generator=g).to(dt)
+        v = torch.randn(1, 1, s, d, generator=g).to(dt)
+        do = torch.randn(1, group, s, d, generator=g).to(dt)
+        oracle.sdpa_reference_route(q[:, :, :256], k[:, :, :256], v[:, :, :256], do[:, :, :256], causal=True)
+    except RuntimeError:
+        dt = torch.float32
+        q, k, v, do = (t.float() for t in (q, k, v, do))
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < min_runs or (time.perf_counter() - t_start) < budget_s:
+        t0 = time.perf_counter()
+        oracle.sdpa_reference_route(q, k, v, do, causal=True)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 50:
+            break
+    per_unit = statistics.median(times)
+    unit_flops = 3.5 * fwd_flops(1, group, s, s, d, True)
+    return unit_flops / per_unit / 1e12, per_unit, ("bf16" if dt == torch.bfloat16 else "fp32"), len(times), torch.get_num_threads()
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU route on the host cores (rank 0 only)."""
+    if rank != 0:
+        return 0
+    g = torch.Generator().manual_seed(0)
+    from oracle import attention_oracle as oracle
+
+    group = CFG["Hq"] // CFG["Hkv"]
+    s, d = CFG["S"], CFG["D"]
+    q = (torch.randn(1, group, s, d, generator=g) * d ** -0.5).bfloat16()
+    k = torch.randn(1, 1, s, d, generator=g).bfloat16()
+    v = torch.randn(1, 1, s, d, generator=g).bfloat16()
+    do = torch.randn(1, group, s, d, generator=g).bfloat16()
+    dtn = "bf16"
+    try:
+        oracle.sdpa_reference_route(q[:, :, :256], k[:, :, :256], v[:, :, :256], do[:, :, :256], causal=True)
+    except RuntimeError:
+        q, k, v, do = (t.float() for t in (q, k, v, do))
+        dtn = "fp32"
+    for _ in range(args.warmup):
+        oracle.sdpa_reference_route(q, k, v, do, causal=True)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.sdpa_reference_route(q, k, v, do, causal=True)
+        times.append(time.perf_counter() - t0)
+    per_unit = statistics.median(times)
+    unit_flops = 3.5 * fwd_flops(1, group, s, s, d, True)
+    tflops = unit_flops / per_unit / 1e12
+    units = CFG["B"] * CFG["Hkv"] * world
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per_unit * units * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtn, "data": "synthetic",
+        "config": {"workload": "GQA causal prefill fwd+bwd B4 Hq32 Hkv8 S4096 D128 per rank",
+                   "global_batch": 4 * world, "seq_len": s, "parallelism": f"units{world}",
+                   "sample": "one (batch, kv-head) unit per step, extrapolated to the job"},
+        "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": f"1 of {units} units per step ({dtn}), "
+                         "reference backend='sdpa' route + autograd"},
+        "e2e": {"value": round(tflops, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- main
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-benchmarks")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    args = ap.parse_args(argv)
+    args.warmup = max(3, args.warmup)
+
+    world, rank, local = init_dist(args)
+    if args.impl == "reference":
+        rc = run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return rc
+
+    from kotflash_b200 import _ext
+
+    _ext.load()  # fail loudly when the kernel library is missing
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    peaks = load_peaks()
+    ms_step, fwd_ms, bwd_ms, clocks = bench_prefill(args, world, rank, local, dtype)
+    b, hq, s, d = CFG["B"], CFG["Hq"], CFG["S"], CFG["D"]
+    f_fwd = fwd_flops(b, hq, s, s, d, True)
+    f_bwd = 2.5 * f_fwd
+    per_rank = f_fwd + f_bwd
+    value = world * per_rank / (ms_step * 1e-3) / 1e12
+
+    e2e = None
+    if not args.no_e2e:
+        e2e_ms, h2d, d2h = bench_prefill_e2e(args, world, rank, dtype)
+        e2e = {"value": round(world * per_rank / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "ms_per_step": round(e2e_ms, 3)}
+
+    peak = peaks["bf16_tflops"]
+    bwd_achieved = f_bwd / (bwd_ms * 1e-3) / 1e12
+    fwd_achieved = f_fwd / (fwd_ms * 1e-3) / 1e12
+    traffic = load_traffic()
+    roofline = {
+        "bound": "tensor", "kernel": "kf_attn_bwd (prep + main + finish launches)",
+        "achieved": round(bwd_achieved, 1), "peak": peak, "unit": "TFLOP/s",
+        "frac": round(bwd_achieved / peak, 4),
+        "traffic": (traffic or {}).get("bwd_main_bytes_per_launch"),
+        "peak_source": f"{peaks['source']} (burst bf16 cuBLAS)",
+        "forward": {"kernel": "kf_attn_fwd", "achieved": round(fwd_achieved, 1),
+                    "frac": round(fwd_achieved / peak, 4),
+                    "traffic": (traffic or {}).get("fwd_bytes_per_launch")},
+        "step_frac": round(value / world / peak, 4),
+    }
+
+    decode = None
+    multi = None
+    if not args.no_decode:
+        if world > 1:
+            multi = bench_decode_multi_gpu(world, rank)
+        elif rank == 0:
+            decode = {"sweep": bench_decode_sweep(peaks), "kv_cache_loop": bench_cache_loop(peaks)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tflops, per_unit, dtn, runs, threads = cpu_unit_sample(args.dtype)
+        cpu = {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{runs} run(s) of one (batch, kv-head) unit of 32 ({dtn}): reference "
+                         f"backend='sdpa' route + autograd, {per_unit:.2f} s/unit"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.dtype, "data": "synthetic",
+            "config": {"workload": "GQA causal prefill fwd+bwd B4 Hq32 Hkv8 S4096 D128 per rank "
+                                   "(BASELINE configs[1])",
+                       "global_batch": 4 * world, "seq_len": s, "head_dim": d,
+                       "parallelism": f"(batch x kv-head) units, {world} rank(s), no collective",
+                       "l2": "inputs larger than L2 (q/dO 134 MB each)"},
+            "frac_of_peak": round(value / world / peak, 4),
+            "roofline": roofline, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": 4 * args.steps,
+            "cpu_baseline": cpu,
+            "decode": decode, "decode_multi_gpu": multi,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -145,3 +145,23 @@ def attention_flops(b: int, hq: int, sq: int, sk: int, d: int, causal: bool) -> 
         pairs = sq * sk
     fwd = 4 * b * hq * d * pairs
     return fwd, int(2.5 * fwd)
+
+
+def sdpa_reference_route(q, k, v, do, *, causal: bool):
+    """The reference's ``backend="sdpa"`` route with autograd, as a timed CPU baseline.
+
+    Restates ``_sdpa`` (kotflash/attention.py:120-135): PyTorch SDPA with
+    native GQA (``enable_gqa=True``) and the default scale left implicit, then
+    autograd for dQ/dK/dV.  Returns (O, dQ, dK, dV).
+    """
+    import torch.nn.functional as F
+
+    q = q.detach().requires_grad_(True)
+    k = k.detach().requires_grad_(True)
+    v = v.detach().requires_grad_(True)
+    kwargs = {"attn_mask": None, "dropout_p": 0.0, "is_causal": causal}
+    if q.shape[1] != k.shape[1]:
+        kwargs["enable_gqa"] = True
+    o = F.scaled_dot_product_attention(q, k, v, **kwargs)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), do)
+    return o.detach(), dq, dk, dv
