@@ -113,6 +113,26 @@ int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
               int num_splits, void* workspace, size_t workspace_bytes,
               void* stream);
 
+/* ---- K3, allocation-free variant ---------------------------------------
+ * No counterpart in the reference: added for callers that cannot allocate
+ * device memory or hand this library a workspace — a host runtime that owns
+ * every device allocation itself (an inference server's memory manager, or an
+ * FFI embedder with a fixed device-memory budget) and gives plugins no
+ * allocator.  Same arguments and results as kf_decode minus the workspace:
+ * the split partials go to one file-scope device array of 8 MiB that every
+ * GPU loading the library holds until exit.  The first call on a device
+ * (with that device current) looks up the array's device address; make that
+ * first call before any stream capture.  num_splits == 0 plans the split
+ * count and lowers it until the partials fit in 8 MiB; an explicit
+ * num_splits whose partials (num_splits * B*Hq*Sq * (D+1) * 4 bytes) exceed
+ * 8 MiB is rejected with KF_ERR_WORKSPACE.  All calls share the array: calls
+ * that overlap on the GPU (different streams or threads) race and must be
+ * serialised by the caller.  Calls no allocator. */
+int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                      const kf_tensor4* new_k, const kf_tensor4* new_v, int64_t past_len,
+                      const kf_tensor4* o, float* lse, int dtype, float scale,
+                      int num_splits, void* stream);
+
 /* ---- K3b: LSE-weighted merge of partial (O, LSE) ------------------------
  * Replaces `_attention_fwd_split_kv_reduce` (triton_forward.py:270-349).
  * part_o: [S, rows, D] fp32, part_lse: [S, rows] fp32, where rows =

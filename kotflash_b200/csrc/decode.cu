@@ -570,3 +570,89 @@ extern "C" int kf_merge_partials(const float* part_o, const float* part_lse, int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == KF_BF16 ? launch_merge<true>(m, st) : launch_merge<false>(m, st);
 }
+
+// ---------------------------------------------------------------------------
+// Decode entry point that allocates nothing.
+//
+// Some callers cannot hand this library a workspace or let it allocate: a host
+// runtime that owns every device allocation itself (an inference server's
+// memory manager, or a JNI/cgo/ctypes embedder with a fixed device-memory
+// budget) and gives plugins no allocator to call.  For them the split partials
+// live in one file-scope device array of kNoAllocScratchBytes.  Every GPU that
+// loads this library holds that array until the process exits.
+//
+// Set-up: the first call on each device, with that device current, asks the
+// runtime for the array's device address (cudaGetSymbolAddress) and caches it
+// per device; make that first call before any stream capture.  Host code must
+// never pass the array's name to a kernel: on the host it is only a stand-in.
+//
+// Sharing: all calls use the same array and it keeps the last call's
+// contents.  Nothing needs clearing (every split writes each of its partial
+// rows before the merge reads them), but calls that overlap on the GPU (two
+// streams, or two threads' streams) race on the array: serialise them.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
+__device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* ptrs[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return kf::set_error(KF_ERR_CUDA, "kf_decode_noalloc: no current CUDA device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || !p)
+      return kf::set_error(KF_ERR_CUDA, "kf_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                           cudaGetErrorString(e));
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return KF_OK;
+}
+
+int64_t effective_splits(int64_t Sk, int64_t s) {
+  const int64_t chunk = cdiv64(cdiv64(Sk, s), 64) * 64;
+  return cdiv64(Sk, chunk);
+}
+}  // namespace
+
+extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                                 const kf_tensor4* new_k, const kf_tensor4* new_v,
+                                 int64_t past_len, const kf_tensor4* o, float* lse, int dtype,
+                                 float scale, int num_splits, void* stream) {
+  if (!q || !k) return kf::set_error(KF_ERR_INVALID, "kf_decode_noalloc: null tensor descriptor");
+  const int64_t B = q->size[0], Hq = q->size[1], Sq = q->size[2], D = q->size[3];
+  const int64_t Hkv = k->size[1], Sk = k->size[2];
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0 || D <= 0)
+    return kf::set_error(KF_ERR_INVALID, "kf_decode_noalloc: dimensions must be non-zero");
+  const size_t per_split = (size_t)(B * Hq * Sq) * (size_t)(D + 1) * sizeof(float);
+  int64_t splits;
+  if (num_splits > 0) {
+    splits = effective_splits(Sk, num_splits);
+    if (splits > 1 && kf_decode_workspace_bytes(B, Hq, Sq, D, (int)splits) > kNoAllocScratchBytes)
+      return kf::set_error(KF_ERR_WORKSPACE,
+                           "kf_decode_noalloc: %lld splits need %zu bytes of scratch, more than "
+                           "the %zu-byte static maximum; pass fewer splits or use kf_decode",
+                           (long long)splits,
+                           kf_decode_workspace_bytes(B, Hq, Sq, D, (int)splits),
+                           kNoAllocScratchBytes);
+  } else {
+    splits = effective_splits(
+        Sk, kf_decode_num_splits(B, Hq, Hkv, Sq, Sk, D, kf::sm_count_current_device()));
+    const int64_t fit = (int64_t)((kNoAllocScratchBytes - 256) / per_split);
+    if (splits > fit) splits = fit >= 2 ? effective_splits(Sk, fit) : 1;
+  }
+  void* scratch = nullptr;
+  if (splits > 1) {
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != KF_OK) return rc;
+  }
+  return kf_decode(q, k, v, new_k, new_v, past_len, o, lse, dtype, scale, (int)splits, scratch,
+                   splits > 1 ? kNoAllocScratchBytes : 0, stream);
+}
