@@ -64,7 +64,9 @@ def pack_partial(o: torch.Tensor, lse: torch.Tensor) -> torch.Tensor:
 def gather_partials(packed: torch.Tensor, group=None) -> Tuple[torch.Tensor, torch.Tensor]:
     """All-gather the packed partials of every rank; returns ([W, rows, D], [W, rows])."""
     world = dist.get_world_size(group)
-    out = torch.empty((world,) + tuple(packed.shape), dtype=packed.dtype, device=packed.device)
+    # concatenated along dim 0 (the form both NCCL and gloo accept)
+    out = torch.empty((world * packed.shape[0],) + tuple(packed.shape[1:]), dtype=packed.dtype,
+                      device=packed.device)
     dist.all_gather_into_tensor(out, packed, group=group)
     d = packed.shape[-1] - 1
     rows = packed[..., 0].numel()
