@@ -16,11 +16,15 @@
 //               every 64-row query block that can see its keys.  Per step:
 //                 S^T  = K Q^T      (SS MMA, M=128 keys, N=64 rows)
 //                 dP^T = V dO^T     (SS MMA)
-//                 softmax warps (thread = key): P^T, dS^T -> TMEM (16-bit) and
-//                 dS^T -> shared memory (128-byte swizzled, q contiguous)
+//                 softmax warps (thread = key), in two phases: P^T as soon as
+//                 S^T is ready, dS^T = P^T (dP^T - Delta) once dP^T is, each
+//                 written to TMEM as 16-bit; dS^T also to shared memory
+//                 (128-byte swizzled, q contiguous)
 //                 dV  += P^T dO     (TS MMA, A = P^T in TMEM)
 //                 dK  += dS^T Q     (TS MMA, A = dS^T in TMEM)
 //                 dQ^T = K^T dS^T   (SS MMA, both operands MN-major)
+//               Issue order dV(s), S^T(s+1), dK(s), dQ^T(s), dP^T(s+1) hides
+//               each softmax phase behind two or three GEMMs.
 //               dQ^T (thread = head-dim lane) is added into an fp32 workspace
 //               with vector atomics by a dedicated warpgroup, double-buffered
 //               in TMEM.  dK/dV accumulate in TMEM for the whole group and are
@@ -57,7 +61,7 @@ struct BwdParams {
 struct __align__(8) BwdBarriers {
   uint64_t kv_full;
   uint64_t qdo_full[kStages], qdo_empty[kStages];
-  uint64_t s_full, ds_full;
+  uint64_t s_ready, dp_ready, p_ready, ds_ready;
   uint64_t dq_full[2], dq_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -124,8 +128,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::mbar_init(&bars->qdo_full[s], 1);
       kf::mbar_init(&bars->qdo_empty[s], 1);
     }
-    kf::mbar_init(&bars->s_full, 1);
-    kf::mbar_init(&bars->ds_full, 128);
+    kf::mbar_init(&bars->s_ready, 1);
+    kf::mbar_init(&bars->dp_ready, 1);
+    kf::mbar_init(&bars->p_ready, 128);
+    kf::mbar_init(&bars->ds_ready, 128);
     for (int s = 0; s < 2; ++s) {
       kf::mbar_init(&bars->dq_full[s], 1);
       kf::mbar_init(&bars->dq_empty[s], 128);
@@ -179,39 +185,70 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const uint32_t idesc_q = kf::make_idesc_f16(BF16, 128, kBM, 1, 1);
       const uint32_t sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
       const uint32_t sq_u = kf::smem_u32(sQ), sdo_u = kf::smem_u32(sdO), sds_u = kf::smem_u32(sdS);
-      bool ok = wait_bar(&bars->kv_full, 0, bars, p.status);
-      for (int s = 0; ok && s < nsteps; ++s) {
-        const int st = s % kStages;
-        if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
-        kf::tc_fence_after();
-        const uint32_t qb = sq_u + st * 2 * QPANEL, dob = sdo_u + st * 2 * QPANEL;
+      auto issue_s = [&](int s) {  // S^T = K Q^T
+        const uint32_t qb = sq_u + (s % kStages) * 2 * QPANEL;
         for (int kk = 0; kk < k_steps; ++kk) {
           const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
           const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
           kf::umma_ss(tmem + 256, kf::make_sdesc(sk_u + ka, 16, 1024),
                       kf::make_sdesc(qb + qa, 16, 1024), idesc_s, kk > 0);
+        }
+      };
+      auto issue_dp = [&](int s) {  // dP^T = V dO^T
+        const uint32_t dob = sdo_u + (s % kStages) * 2 * QPANEL;
+        for (int kk = 0; kk < k_steps; ++kk) {
+          const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
+          const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
           kf::umma_ss(tmem + 320, kf::make_sdesc(sv_u + ka, 16, 1024),
                       kf::make_sdesc(dob + qa, 16, 1024), idesc_s, kk > 0);
         }
-        kf::umma_commit(&bars->s_full);
-        if (!(ok = wait_bar(&bars->ds_full, s & 1, bars, p.status))) break;
+      };
+      // Issue order per step s:  dV(s)  S^T(s+1)  dK(s)  dQ^T(s)  dP^T(s+1)
+      // so the softmax's P phase of step s+1 overlaps dK/dQ^T/dP^T and its dS
+      // phase of step s overlaps dV(s)/S^T(s+1).
+      bool ok = wait_bar(&bars->kv_full, 0, bars, p.status) &&
+                wait_bar(&bars->qdo_full[0], 0, bars, p.status);
+      if (ok) {
         kf::tc_fence_after();
-        for (int kk = 0; kk < kBM / 16; ++kk) {
-          const uint32_t acc = (s > 0 || kk > 0);
+        issue_s(0);
+        kf::umma_commit(&bars->s_ready);
+        issue_dp(0);
+        kf::umma_commit(&bars->dp_ready);
+      }
+      for (int s = 0; ok && s < nsteps; ++s) {
+        const int st = s % kStages;
+        const uint32_t qb = sq_u + st * 2 * QPANEL, dob = sdo_u + st * 2 * QPANEL;
+        const bool more = s + 1 < nsteps;
+        if (!(ok = wait_bar(&bars->p_ready, s & 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        for (int kk = 0; kk < kBM / 16; ++kk)
           kf::umma_ts(tmem + 0, tmem + 256 + kk * 8, kf::make_sdesc(dob + kk * 2048, QPANEL, 1024),
-                      idesc_kv, acc);
-          kf::umma_ts(tmem + 128, tmem + 320 + kk * 8, kf::make_sdesc(qb + kk * 2048, QPANEL, 1024),
-                      idesc_kv, acc);
+                      idesc_kv, (s > 0 || kk > 0));
+        if (more) {
+          if (!(ok = wait_bar(&bars->qdo_full[(s + 1) % kStages], ((s + 1) / kStages) & 1, bars,
+                              p.status)))
+            break;
+          kf::tc_fence_after();
+          issue_s(s + 1);
+          kf::umma_commit(&bars->s_ready);
         }
+        if (!(ok = wait_bar(&bars->ds_ready, s & 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        for (int kk = 0; kk < kBM / 16; ++kk)
+          kf::umma_ts(tmem + 128, tmem + 320 + kk * 8, kf::make_sdesc(qb + kk * 2048, QPANEL, 1024),
+                      idesc_kv, (s > 0 || kk > 0));
+        kf::umma_commit(&bars->qdo_empty[st]);
         const int buf = s & 1;
         if (!(ok = wait_bar(&bars->dq_empty[buf], ((s >> 1) & 1) ^ 1, bars, p.status))) break;
         kf::tc_fence_after();
-        for (int kk = 0; kk < kBN / 16; ++kk) {
+        for (int kk = 0; kk < kBN / 16; ++kk)
           kf::umma_ss(tmem + 384 + buf * 64, kf::make_sdesc(sk_u + kk * 2048, KPANEL, 1024),
                       kf::make_sdesc(sds_u + kk * 2048, KPANEL, 1024), idesc_q, kk > 0);
-        }
         kf::umma_commit(&bars->dq_full[buf]);
-        kf::umma_commit(&bars->qdo_empty[st]);
+        if (more) {
+          issue_dp(s + 1);
+          kf::umma_commit(&bars->dp_ready);
+        }
       }
       kf::umma_commit(&bars->mma_done);
     }
@@ -224,38 +261,45 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     for (int s = 0; ok && s < nsteps; ++s) {
       const int st = s % kStages;
       if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
-      if (!(ok = wait_bar(&bars->s_full, s & 1, bars, p.status))) break;
+      if (!(ok = wait_bar(&bars->s_ready, s & 1, bars, p.status))) break;
       kf::tc_fence_after();
       int h, i;
       step_coords(s, h, i);
-      uint32_t sr[64], dr[64];
+      uint32_t sr[64];
       kf::tmem_ld32(lane_base + 256, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
       kf::tmem_ld32(lane_base + 288, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      kf::tmem_ld32(lane_base + 320, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      kf::tmem_ld32(lane_base + 352, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
       kf::tmem_wait_ld();
       const float* lse2 = sLD + st * 2 * kBM;
       const float* dlt = lse2 + kBM;
       const int q0 = i * kBM;
-      // visible iff key < Sk and (not causal or key <= q)
-      const int first_q = p.causal ? key - q0 : 0;  // columns c >= first_q are visible
+      // visible iff key < Sk and (not causal or key <= q): columns c >= first_q
+      const int first_q = p.causal ? key - q0 : 0;
       const bool key_ok = key < p.Sk;
-      uint32_t pk[32], dk[32];
+      float pr[kBM];
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < kBM; c += 2) {
-        float pr[2], dsv[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int cc = c + e;
-          const bool vis = key_ok && cc >= first_q;
-          const float x = __uint_as_float(sr[cc]) * p.scale_log2 - lse2[cc];
-          pr[e] = vis ? kf::ex2(x) : 0.f;
-          dsv[e] = pr[e] * (__uint_as_float(dr[cc]) - dlt[cc]);
-        }
-        pk[c / 2] = kf::pack2<BF16>(pr[0], pr[1]);
-        dk[c / 2] = kf::pack2<BF16>(dsv[0], dsv[1]);
+      for (int c = 0; c < kBM; ++c) {
+        const float x = __uint_as_float(sr[c]) * p.scale_log2 - lse2[c];
+        pr[c] = (key_ok && c >= first_q) ? kf::ex2(x) : 0.f;
       }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) pk[c] = kf::pack2<BF16>(pr[2 * c], pr[2 * c + 1]);
       kf::tmem_st32(lane_base + 256, pk);
+      kf::tmem_wait_st();
+      kf::tc_fence_before();
+      kf::mbar_arrive(&bars->p_ready);
+
+      if (!(ok = wait_bar(&bars->dp_ready, s & 1, bars, p.status))) break;
+      kf::tc_fence_after();
+      uint32_t dr[64];
+      kf::tmem_ld32(lane_base + 320, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
+      kf::tmem_ld32(lane_base + 352, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      kf::tmem_wait_ld();
+      uint32_t dk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        dk[c] = kf::pack2<BF16>(pr[2 * c] * (__uint_as_float(dr[2 * c]) - dlt[2 * c]),
+                                pr[2 * c + 1] * (__uint_as_float(dr[2 * c + 1]) - dlt[2 * c + 1]));
       kf::tmem_st32(lane_base + 320, dk);
       // dS^T row -> shared memory, 128-byte swizzle (16-byte chunk c at c ^ (row & 7))
       uint8_t* row_ptr = sdS + kr * 128;
@@ -266,7 +310,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::fence_proxy_async_smem();
       kf::tmem_wait_st();
       kf::tc_fence_before();
-      kf::mbar_arrive(&bars->ds_full);
+      kf::mbar_arrive(&bars->ds_ready);
     }
   } else {
     // ------------------------------------------------------------ dQ drain (thread = head-dim lane)
