@@ -25,13 +25,17 @@
 //                 dQ^T = K^T dS^T   (SS MMA, both operands MN-major)
 //               Issue order dV(s), S^T(s+1), dK(s), dQ^T(s), dP^T(s+1) hides
 //               each softmax phase behind two or three GEMMs.
-//               dQ^T (thread = head-dim lane) is added into an fp32 workspace
-//               with vector atomics by a dedicated warpgroup, double-buffered
-//               in TMEM.  dK/dV accumulate in TMEM for the whole group and are
+//               dQ^T (thread = head-dim lane, double-buffered in TMEM) is
+//               staged in 128-byte swizzled shared memory by a dedicated
+//               warpgroup and added into the fp32 workspace with TMA
+//               reduce-add (cp.reduce.async.bulk.tensor), off the LSU path.  dK/dV accumulate in TMEM for the whole group and are
 //               written once, so no dK/dV partial buffers exist.
 //   3. finish : dQ = scale * workspace, cast to the input dtype.
 // Tensor memory (512 columns): dV [0,128) dK [128,256) S^T [256,320)
 // dP^T [320,384) dQ^T buffers [384,448) [448,512).
+// Warps: 0-7 softmax (two warpgroups split the 64 query columns), 8-11 dQ
+// drain, 12 TMA producer, 13 TMEM allocator + MMA issuer; 0-7 also write the
+// dV (warps 0-3) and dK (warps 4-7) epilogue.
 #include <math.h>
 
 #include "kf_host.h"
@@ -42,7 +46,7 @@ namespace {
 constexpr int kBM = 64;    // query rows per step
 constexpr int kBN = 128;   // keys per CTA
 constexpr int kStages = 2;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;  // 14 warps
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
@@ -98,7 +102,7 @@ template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
-           const BwdParams p) {
+           const __grid_constant__ CUtensorMap map_dq, const BwdParams p) {
   constexpr int KPANEL = kBN * 128;  // 16 KB: 128 rows x 64 columns
   constexpr int QPANEL = kBM * 128;  // 8 KB: 64 rows x 64 columns
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -109,7 +113,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   uint8_t* sQ = sV + 2 * KPANEL;                    // [stage][2 panels]
   uint8_t* sdO = sQ + kStages * 2 * QPANEL;         // [stage][2 panels]
   uint8_t* sdS = sdO + kStages * 2 * QPANEL;        // 128 rows x 128 B
-  float* sLD = reinterpret_cast<float*>(sdS + KPANEL);  // [stage][lse2 64 | delta 64]
+  uint8_t* sDQ = sdS + KPANEL;                      // [2 buffers][2 halves][D rows][32 fp32]
+  float* sLD = reinterpret_cast<float*>(sDQ + 2 * 2 * 128 * 128);  // [stage][lse2 64 | delta 64]
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(sLD + kStages * 2 * kBM);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -130,8 +135,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     }
     kf::mbar_init(&bars->s_ready, 1);
     kf::mbar_init(&bars->dp_ready, 1);
-    kf::mbar_init(&bars->p_ready, 128);
-    kf::mbar_init(&bars->ds_ready, 128);
+    kf::mbar_init(&bars->p_ready, 256);
+    kf::mbar_init(&bars->ds_ready, 256);
     for (int s = 0; s < 2; ++s) {
       kf::mbar_init(&bars->dq_full[s], 1);
       kf::mbar_init(&bars->dq_empty[s], 128);
@@ -140,7 +145,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     bars->abort_flag = 0;
     kf::fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     kf::tmem_alloc(&bars->tmem_base, 512);
     kf::tmem_relinquish();
   }
@@ -154,7 +159,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     i = i0 + s % nq_steps;
   };
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && nsteps > 0) {
       kf::mbar_arrive_expect_tx(&bars->kv_full, 4 * KPANEL);
@@ -177,7 +182,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         bulk_load(sLD + st * 2 * kBM + kBM, p.delta + row_off, kBM * 4, &bars->qdo_full[st]);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nsteps > 0) {
       const uint32_t idesc_s = kf::make_idesc_f16(BF16, 128, kBM, 0, 0);
@@ -252,11 +257,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       }
       kf::umma_commit(&bars->mma_done);
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ P / dS (thread = key)
-    const int kr = warp * 32 + lane;
+    // two warpgroups: wg 0 takes query columns [0, 32), wg 1 takes [32, 64)
+    const int wg = warp >> 2;
+    const int c0 = wg * 32;
+    const int kr = (warp & 3) * 32 + lane;
     const int key = n * kBN + kr;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
     for (int s = 0; ok && s < nsteps; ++s) {
       const int st = s % kStages;
@@ -265,57 +273,57 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::tc_fence_after();
       int h, i;
       step_coords(s, h, i);
-      uint32_t sr[64];
-      kf::tmem_ld32(lane_base + 256, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      kf::tmem_ld32(lane_base + 288, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      uint32_t sr[32];
+      kf::tmem_ld32(lane_base + 256 + c0, sr);
       kf::tmem_wait_ld();
-      const float* lse2 = sLD + st * 2 * kBM;
-      const float* dlt = lse2 + kBM;
-      const int q0 = i * kBM;
+      const float* lse2 = sLD + st * 2 * kBM + c0;
+      const float* dlt = sLD + st * 2 * kBM + kBM + c0;
+      const int q0 = i * kBM + c0;
       // visible iff key < Sk and (not causal or key <= q): columns c >= first_q
       const int first_q = p.causal ? key - q0 : 0;
       const bool key_ok = key < p.Sk;
-      float pr[kBM];
-      uint32_t pk[32];
+      float pr[32];
+      uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < kBM; ++c) {
+      for (int c = 0; c < 32; ++c) {
         const float x = __uint_as_float(sr[c]) * p.scale_log2 - lse2[c];
         pr[c] = (key_ok && c >= first_q) ? kf::ex2(x) : 0.f;
       }
 #pragma unroll
-      for (int c = 0; c < 32; ++c) pk[c] = kf::pack2<BF16>(pr[2 * c], pr[2 * c + 1]);
-      kf::tmem_st32(lane_base + 256, pk);
+      for (int c = 0; c < 16; ++c) pk[c] = kf::pack2<BF16>(pr[2 * c], pr[2 * c + 1]);
+      kf::tmem_st16(lane_base + 256 + wg * 16, pk);
       kf::tmem_wait_st();
       kf::tc_fence_before();
       kf::mbar_arrive(&bars->p_ready);
 
       if (!(ok = wait_bar(&bars->dp_ready, s & 1, bars, p.status))) break;
       kf::tc_fence_after();
-      uint32_t dr[64];
-      kf::tmem_ld32(lane_base + 320, *reinterpret_cast<uint32_t(*)[32]>(&dr[0]));
-      kf::tmem_ld32(lane_base + 352, *reinterpret_cast<uint32_t(*)[32]>(&dr[32]));
+      uint32_t dr[32];
+      kf::tmem_ld32(lane_base + 320 + c0, dr);
       kf::tmem_wait_ld();
-      uint32_t dk[32];
+      uint32_t dk[16];
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
+      for (int c = 0; c < 16; ++c)
         dk[c] = kf::pack2<BF16>(pr[2 * c] * (__uint_as_float(dr[2 * c]) - dlt[2 * c]),
                                 pr[2 * c + 1] * (__uint_as_float(dr[2 * c + 1]) - dlt[2 * c + 1]));
-      kf::tmem_st32(lane_base + 320, dk);
+      kf::tmem_st16(lane_base + 320 + wg * 16, dk);
       // dS^T row -> shared memory, 128-byte swizzle (16-byte chunk c at c ^ (row & 7))
       uint8_t* row_ptr = sdS + kr * 128;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        *reinterpret_cast<uint4*>(row_ptr + ((c8 ^ (kr & 7)) << 4)) =
-            make_uint4(dk[4 * c8], dk[4 * c8 + 1], dk[4 * c8 + 2], dk[4 * c8 + 3]);
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(row_ptr + (((wg * 4 + j) ^ (kr & 7)) << 4)) =
+            make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
       kf::fence_proxy_async_smem();
       kf::tmem_wait_st();
       kf::tc_fence_before();
       kf::mbar_arrive(&bars->ds_ready);
     }
-  } else {
+  } else if (warp < 12) {
     // ------------------------------------------------------------ dQ drain (thread = head-dim lane)
-    const int dl = (warp - 4) * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+    // TMEM -> swizzled shared staging tile -> TMA reduce-add into the fp32 workspace
+    const int dl = (warp - 8) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 8) * 32) << 16);
+    const int d_rows = p.D;                 // multiple of 8, so halves stay 1024-aligned
     bool ok = true;
     for (int s = 0; ok && s < nsteps; ++s) {
       const int buf = s & 1;
@@ -327,17 +335,33 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::tmem_wait_ld();
       kf::tc_fence_before();
       kf::mbar_arrive(&bars->dq_empty[buf]);
-      if (dl < p.D) {
+      // staging buffer `buf` was last used two steps ago: let that reduce finish reading
+      if (dl == 0) kf::bulk_wait_group_read<1>();
+      kf::named_bar_sync(1, 128);
+      uint8_t* stage = sDQ + buf * 2 * 128 * 128;
+      if (dl < d_rows) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint8_t* row_ptr = stage + h * d_rows * 128 + dl * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(row_ptr + ((c ^ (dl & 7)) << 4)) =
+                make_uint4(v[h * 32 + 4 * c], v[h * 32 + 4 * c + 1], v[h * 32 + 4 * c + 2],
+                           v[h * 32 + 4 * c + 3]);
+        }
+      }
+      kf::fence_proxy_async_smem();
+      kf::named_bar_sync(1, 128);
+      if (dl == 0) {
         int h, i;
         step_coords(s, h, i);
-        float4* dst = reinterpret_cast<float4*>(
-            p.dq_acc + ((((int64_t)b * p.Hq + h) * p.nqb + i) * p.D + dl) * kBM);
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          atomicAdd(dst + c, make_float4(__uint_as_float(v[4 * c]), __uint_as_float(v[4 * c + 1]),
-                                         __uint_as_float(v[4 * c + 2]), __uint_as_float(v[4 * c + 3])));
+        const int row0 = (int)((((int64_t)b * p.Hq + h) * p.nqb + i) * p.D);
+        kf::tma_reduce_add_2d(&map_dq, stage, 0, row0);
+        kf::tma_reduce_add_2d(&map_dq, stage + d_rows * 128, 32, row0);
+        kf::bulk_commit_group();
       }
     }
+    if (dl == 0) kf::bulk_wait_group<0>();
   }
 
   // ---------------------------------------------------------- dK / dV epilogue
@@ -378,7 +402,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
 
   kf::tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     kf::tc_fence_after();
     kf::tmem_dealloc(tmem, 512);
   }
@@ -505,7 +529,8 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   int rc = kf::check_launch("kf_attn_bwd prep");
   if (rc) return rc;
 
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdq;
+  if ((rc = kf::encode_tmap_2d_f32(&mdq, dq_acc, (int64_t)B * Hq * nqb * D, kBM, 32, D))) return rc;
   if ((rc = kf::encode_tmap_4d(&mq, q, 64, kBM))) return rc;
   if ((rc = kf::encode_tmap_4d(&mdo, dout, 64, kBM))) return rc;
   if ((rc = kf::encode_tmap_4d(&mk, k, 64, kBN))) return rc;
@@ -536,12 +561,12 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   p.scale = scale;
   p.status = status;
   const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 128 * 128 +
-                      kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
+                      2 * 2 * 128 * 128 + kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
   auto kern = bwd_kernel<BF16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
   const int64_t grid = (int64_t)B * Hkv * nkb;
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, p);
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, p);
   if ((rc = kf::check_launch("kf_attn_bwd main"))) return rc;
 
   FinishArgs fa;

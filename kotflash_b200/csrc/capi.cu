@@ -78,6 +78,23 @@ int encode_tmap_4d(CUtensorMap* map, const kf_tensor4* t, int box_inner, int box
   return KF_OK;
 }
 
+int encode_tmap_2d_f32(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int box_cols,
+                       int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return set_error(KF_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (!aligned16(ptr) || (cols * 4) % 16 != 0)
+    return set_error(KF_ERR_INVALID, "fp32 TMA view needs 16-byte aligned base and rows");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KF_ERR_CUDA, "cuTensorMapEncodeTiled (fp32) failed (%d)", (int)r);
+  return KF_OK;
+}
+
 int sm_count_current_device() {
   static int cache[64] = {0};
   int dev = 0;

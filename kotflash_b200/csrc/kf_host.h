@@ -23,6 +23,12 @@ int check_launch(const char* what);
 // as zero.  Returns KF_OK or an error code with the message recorded.
 int encode_tmap_4d(CUtensorMap* map, const kf_tensor4* t, int box_inner, int box_rows);
 
+// Encode a 2-D tiled TMA descriptor over a row-major fp32 matrix
+// [rows][cols] (cols contiguous) with a (box_cols x box_rows) box and 128-byte
+// swizzle (box_cols * 4 must be <= 128).
+int encode_tmap_2d_f32(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int box_cols,
+                       int box_rows);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int sm_count_current_device();

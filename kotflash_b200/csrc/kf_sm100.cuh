@@ -106,6 +106,29 @@ KF_DEVI void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, 
       : "memory");
 }
 
+// 2-D tiled reduce-add of an fp32 tile, this CTA's shared memory -> global,
+// tracked by the bulk-async group of the issuing thread.
+KF_DEVI void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%1, %2}], [%3];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(smem_u32(smem_src))
+      : "memory");
+}
+KF_DEVI void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+KF_DEVI void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+KF_DEVI void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Named barrier among `nthreads` threads (a multiple of 32).
+KF_DEVI void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 // Tensor memory address: bits [31:16] lane, [15:0] column.
 KF_DEVI void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
