@@ -98,7 +98,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-template <bool BF16>
+template <bool BF16, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
@@ -124,8 +124,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   const int i0 = p.causal ? min((n * kBN) / kBM, p.nqb) : 0;
   const int nq_steps = p.nqb - i0;
   const int nsteps = p.G * nq_steps;
-  const int d_pad16 = (p.D + 15) & ~15;
-  const int k_steps = d_pad16 / 16;
+  constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
 
   if (tid == 0) {
     kf::mbar_init(&bars->kv_full, 1);
@@ -190,9 +189,12 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const uint32_t idesc_q = kf::make_idesc_f16(BF16, 128, kBM, 1, 1);
       const uint32_t sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
       const uint32_t sq_u = kf::smem_u32(sQ), sdo_u = kf::smem_u32(sdO), sds_u = kf::smem_u32(sdS);
+      // Each GEMM is one straight-line run of MMAs (compile-time trip counts):
+      // branches between consecutive tcgen05.mma slow their issue down.
       auto issue_s = [&](int s) {  // S^T = K Q^T
         const uint32_t qb = sq_u + (s % kStages) * 2 * QPANEL;
-        for (int kk = 0; kk < k_steps; ++kk) {
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
           const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
           const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
           kf::umma_ss(tmem + 256, kf::make_sdesc(sk_u + ka, 16, 1024),
@@ -201,7 +203,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       };
       auto issue_dp = [&](int s) {  // dP^T = V dO^T
         const uint32_t dob = sdo_u + (s % kStages) * 2 * QPANEL;
-        for (int kk = 0; kk < k_steps; ++kk) {
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
           const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
           const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
           kf::umma_ss(tmem + 320, kf::make_sdesc(sv_u + ka, 16, 1024),
@@ -226,6 +229,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         const bool more = s + 1 < nsteps;
         if (!(ok = wait_bar(&bars->p_ready, s & 1, bars, p.status))) break;
         kf::tc_fence_after();
+#pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk)
           kf::umma_ts(tmem + 0, tmem + 256 + kk * 8, kf::make_sdesc(dob + kk * 2048, QPANEL, 1024),
                       idesc_kv, (s > 0 || kk > 0));
@@ -239,6 +243,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         }
         if (!(ok = wait_bar(&bars->ds_ready, s & 1, bars, p.status))) break;
         kf::tc_fence_after();
+#pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk)
           kf::umma_ts(tmem + 128, tmem + 320 + kk * 8, kf::make_sdesc(qb + kk * 2048, QPANEL, 1024),
                       idesc_kv, (s > 0 || kk > 0));
@@ -246,6 +251,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         const int buf = s & 1;
         if (!(ok = wait_bar(&bars->dq_empty[buf], ((s >> 1) & 1) ^ 1, bars, p.status))) break;
         kf::tc_fence_after();
+#pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           kf::umma_ss(tmem + 384 + buf * 64, kf::make_sdesc(sk_u + kk * 2048, KPANEL, 1024),
                       kf::make_sdesc(sds_u + kk * 2048, KPANEL, 1024), idesc_q, kk > 0);
@@ -489,6 +495,36 @@ bool rows16(const kf_tensor4* t) {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+template <bool BF16, int KS>
+int launch_bwd_main(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                    const CUtensorMap& mdo, const CUtensorMap& mdq, const BwdParams& p,
+                    cudaStream_t st) {
+  const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 128 * 128 +
+                      2 * 2 * 128 * 128 + kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
+  auto kern = bwd_kernel<BF16, KS>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
+  const int64_t grid = (int64_t)p.B * p.Hkv * p.nkb;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, p);
+  return kf::check_launch("kf_attn_bwd main");
+}
+
+template <bool BF16>
+int dispatch_bwd_main(int ks, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                      const CUtensorMap& mdo, const CUtensorMap& mdq, const BwdParams& p,
+                      cudaStream_t st) {
+  switch (ks) {
+    case 1: return launch_bwd_main<BF16, 1>(mq, mk, mv, mdo, mdq, p, st);
+    case 2: return launch_bwd_main<BF16, 2>(mq, mk, mv, mdo, mdq, p, st);
+    case 3: return launch_bwd_main<BF16, 3>(mq, mk, mv, mdo, mdq, p, st);
+    case 4: return launch_bwd_main<BF16, 4>(mq, mk, mv, mdo, mdq, p, st);
+    case 5: return launch_bwd_main<BF16, 5>(mq, mk, mv, mdo, mdq, p, st);
+    case 6: return launch_bwd_main<BF16, 6>(mq, mk, mv, mdo, mdq, p, st);
+    case 7: return launch_bwd_main<BF16, 7>(mq, mk, mv, mdo, mdq, p, st);
+    default: return launch_bwd_main<BF16, 8>(mq, mk, mv, mdo, mdq, p, st);
+  }
+}
+
 template <bool BF16>
 int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const kf_tensor4* o,
             const float* lse, const kf_tensor4* dout, const kf_tensor4* dq, const kf_tensor4* dk,
@@ -560,14 +596,7 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   p.scale_log2 = scale * kLog2e;
   p.scale = scale;
   p.status = status;
-  const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 128 * 128 +
-                      2 * 2 * 128 * 128 + kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
-  auto kern = bwd_kernel<BF16>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
-  const int64_t grid = (int64_t)B * Hkv * nkb;
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, p);
-  if ((rc = kf::check_launch("kf_attn_bwd main"))) return rc;
+  if ((rc = dispatch_bwd_main<BF16>((D + 15) / 16, mq, mk, mv, mdo, mdq, p, st))) return rc;
 
   FinishArgs fa;
   fa.acc = dq_acc;

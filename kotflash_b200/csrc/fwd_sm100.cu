@@ -111,7 +111,7 @@ __device__ __forceinline__ TileInfo tile_info(const FwdParams& p) {
   return ti;
 }
 
-template <bool BF16, int NP>
+template <bool BF16, int NP, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const FwdParams p) {
@@ -128,8 +128,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const TileInfo ti = tile_info(p);
   const int nblk = ti.n_blocks;
-  const int d_pad16 = (p.D + 15) & ~15;
-  const int k_steps = d_pad16 / 16;
+  constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
 
   if (tid == 0) {
     kf::mbar_init(&bars->q_full, 1);
@@ -192,9 +191,12 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const uint32_t idesc_pv = kf::make_idesc_f16(BF16, kBlockM, d_pad16, 0, 1);
       const uint32_t sq_u = kf::smem_u32(sQ), sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
       const int nt = ti.valid[1] ? 2 : 1;
+      // Each GEMM is one straight-line run of MMAs (compile-time trip counts):
+      // branches between consecutive tcgen05.mma slow their issue down.
       auto issue_qk = [&](int t, int j) {
         const uint32_t qb = sq_u + t * TILE, kb = sk_u + (j % kStages) * TILE;
-        for (int kk = 0; kk < k_steps; ++kk) {
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
           const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
           kf::umma_ss(tmem + t * 128, kf::make_sdesc(qb + off, 16, 1024),
                       kf::make_sdesc(kb + off, 16, 1024), idesc_qk, kk > 0);
@@ -202,6 +204,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       };
       auto issue_pv = [&](int t, int j) {
         const uint32_t vb = sv_u + (j % kStages) * TILE;
+#pragma unroll
         for (int kk = 0; kk < kBlockN / 16; ++kk) {
           kf::umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
                       kf::make_sdesc(vb + kk * 2048, PANEL, 1024), idesc_pv, (j > 0 || kk > 0));
@@ -357,18 +360,34 @@ bool rows16(const kf_tensor4* t) {
   return true;
 }
 
-template <bool BF16, int NP>
+template <bool BF16, int KS>
 int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                const FwdParams& p, cudaStream_t st) {
+  constexpr int NP = KS > 4 ? 2 : 1;
   constexpr int TILE = NP * kBlockM * 128;
   const size_t smem = 1024 + (size_t)(2 + 2 * kStages) * TILE + sizeof(FwdBarriers);
-  auto kern = fwd_kernel<BF16, NP>;
+  auto kern = fwd_kernel<BF16, NP, KS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: cannot reserve %zu bytes of shared memory", smem);
   const int64_t grid = (int64_t)p.B * p.Hkv * p.ctas_per_kvh;
   kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, p);
   return kf::check_launch("kf_attn_fwd");
+}
+
+template <bool BF16>
+int dispatch_fwd(int ks, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                 const FwdParams& p, cudaStream_t st) {
+  switch (ks) {
+    case 1: return launch_fwd<BF16, 1>(mq, mk, mv, p, st);
+    case 2: return launch_fwd<BF16, 2>(mq, mk, mv, p, st);
+    case 3: return launch_fwd<BF16, 3>(mq, mk, mv, p, st);
+    case 4: return launch_fwd<BF16, 4>(mq, mk, mv, p, st);
+    case 5: return launch_fwd<BF16, 5>(mq, mk, mv, p, st);
+    case 6: return launch_fwd<BF16, 6>(mq, mk, mv, p, st);
+    case 7: return launch_fwd<BF16, 7>(mq, mk, mv, p, st);
+    default: return launch_fwd<BF16, 8>(mq, mk, mv, p, st);
+  }
 }
 
 }  // namespace
@@ -425,8 +444,7 @@ extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   if ((int64_t)p.B * p.Hkv * p.ctas_per_kvh > 0x7fffffffLL)
     return set_error(KF_ERR_UNSUPPORTED, "kf_attn_fwd: grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool two_panels = D > 64;
-  if (dtype == KF_BF16)
-    return two_panels ? launch_fwd<true, 2>(mq, mk, mv, p, st) : launch_fwd<true, 1>(mq, mk, mv, p, st);
-  return two_panels ? launch_fwd<false, 2>(mq, mk, mv, p, st) : launch_fwd<false, 1>(mq, mk, mv, p, st);
+  const int ks = (int)((D + 15) / 16);
+  return dtype == KF_BF16 ? dispatch_fwd<true>(ks, mq, mk, mv, p, st)
+                          : dispatch_fwd<false>(ks, mq, mk, mv, p, st);
 }
