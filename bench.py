@@ -497,6 +497,33 @@ def run_reference(args, world, rank):
     return 0
 
 
+def run_decode_case(args, world, rank):
+    """One decode shape, plain launches (no graph): for profiling and quick timing."""
+    from kotflash_b200.attention import _decode_forward
+
+    sq, sk = (int(x) for x in args.decode_case.split(","))
+    g = torch.Generator(device="cuda").manual_seed(sk + sq)
+    k = torch.randn(2, 2, sk, 64, device="cuda", generator=g).half()
+    v = torch.randn(2, 2, sk, 64, device="cuda", generator=g).half()
+    q = torch.randn(2, 8, sq, 64, device="cuda", generator=g).half()
+    for _ in range(args.warmup):
+        _decode_forward(q, k, v, scale=0.125, want_lse=False)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        _decode_forward(q, k, v, scale=0.125, want_lse=False)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    if rank == 0:
+        alg = 1024 * sk + 4096 * sq + 64 * sq
+        print(json.dumps({"decode_case": [sq, sk], "us_per_call": round(ms * 1e3, 2),
+                          "hbm_gbs": round(alg / (ms * 1e-3) / 1e9, 1),
+                          "note": "plain launches incl. host overhead; inputs L2-warm when < 126 MB"}))
+    return 0
+
+
 # --------------------------------------------------------------------------- main
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -509,6 +536,9 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--decode-case", default=None, metavar="SQ,SK",
+                    help="time only the split-KV decode config (B2 Hq8 Hkv2 D64 fp16) at one "
+                         "(Sq, Sk) with --warmup/--steps plain launches; prints one JSON line")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
 
@@ -524,6 +554,8 @@ def main(argv=None) -> int:
     from kotflash_b200 import _ext
 
     _ext.load()  # fail loudly when the kernel library is missing
+    if args.decode_case:
+        return run_decode_case(args, world, rank)
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     peaks = load_peaks()
     ms_step, fwd_ms, bwd_ms, clocks = bench_prefill(args, world, rank, local, dtype)
