@@ -56,7 +56,6 @@ struct __align__(8) FwdBarriers {
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[2], p_full[2];
-  uint64_t turn[2];  // softmax warpgroups take turns on the exp section
   uint64_t o_final;
   uint32_t tmem_base;
   int abort_flag;
@@ -142,7 +141,6 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     for (int t = 0; t < 2; ++t) {
       kf::mbar_init(&bars->s_full[t], 1);
       kf::mbar_init(&bars->p_full[t], 128);
-      kf::mbar_init(&bars->turn[t], 128);
     }
     kf::mbar_init(&bars->o_final, 1);
     bars->abort_flag = 0;
@@ -254,10 +252,6 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int row = ti.row0[t] + r;
     float m_ref = -INFINITY, l_sum = 0.f;
     bool ok = ti.valid[t] != 0;
-    // With two tiles the warpgroups alternate on the MUFU-heavy exp section:
-    // tile 0 goes first, each hands the turn to the other when done.
-    const bool alternate = ti.valid[1] != 0;
-    if (alternate && t == 1) kf::mbar_arrive(&bars->turn[0]);
     for (int j = 0; ok && j < nblk; ++j) {
       if (!(ok = wait_bar(&bars->s_full[t], j & 1, bars, p.status))) break;
       kf::tc_fence_after();
@@ -267,33 +261,24 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
       kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
       kf::tmem_wait_ld();
+      float x[128];
       const int key0 = j * kBlockN;
       const bool need_mask = (key0 + kBlockN > p.Sk) || (p.causal && key0 + kBlockN - 1 > ti.row0[t]);
-      // Scores stay raw; the scale is folded into one FFMA ahead of ex2.  For
-      // a negative scale the scores are negated so the row maximum is still
-      // taken on the value that ends up largest.  Reductions use 8
-      // independent accumulators to keep dependent chains short.
-      const float sc = fabsf(p.scale_log2);
-      float v[128];
-#pragma unroll
-      for (int c = 0; c < 128; ++c) v[c] = __uint_as_float(sr[c]);
-      if (p.scale_log2 < 0.f) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) v[c] = -v[c];
-      }
+      float mx = -INFINITY;
       if (need_mask) {
         const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : kBlockN);
 #pragma unroll
-        for (int c = 0; c < 128; ++c) v[c] = c < lim ? v[c] : -INFINITY;
+        for (int c = 0; c < 128; ++c) {
+          x[c] = c < lim ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] = __uint_as_float(sr[c]) * p.scale_log2;
+          mx = fmaxf(mx, x[c]);
+        }
       }
-      float m8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = v[i];
-#pragma unroll
-      for (int c = 8; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], v[c]);
-      const float mx_raw = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      const float mx = mx_raw == -INFINITY ? -INFINITY : mx_raw * sc;
       float alpha = 1.f;
       bool rescale_o = false;
       if (j == 0) {
@@ -305,46 +290,17 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       }
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
       l_sum *= alpha;
-      if (alternate && !(ok = wait_bar(&bars->turn[t], j & 1, bars, p.status))) break;
-      float s8[8];
+      uint32_t pk[64];
+      float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
-      // P in 32-column chunks (16 packed registers live at a time), written
-      // over the first 64 columns of this tile's S region.
-      if (sc > 0.f) {
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int c0 = ch * 32 + 2 * c;
-            const float y0 = fmaf(v[c0], sc, -m_use), y1 = fmaf(v[c0 + 1], sc, -m_use);
-            const float p0 = kf::ex2(y0);
-            const float p1 = kf::ex2(y1);
-            s8[(2 * c) & 7] += p0;
-            s8[(2 * c + 1) & 7] += p1;
-            pk[c] = kf::pack2<BF16>(p0, p1);
-          }
-          kf::tmem_st16(lane_base + s_col + ch * 16, pk);
-        }
-      } else {  // scale == 0: every visible key has weight 1
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int c0 = ch * 32 + 2 * c;
-            const float p0 = v[c0] == -INFINITY ? 0.f : 1.f;
-            const float p1 = v[c0 + 1] == -INFINITY ? 0.f : 1.f;
-            s8[(2 * c) & 7] += p0;
-            s8[(2 * c + 1) & 7] += p1;
-            pk[c] = kf::pack2<BF16>(p0, p1);
-          }
-          kf::tmem_st16(lane_base + s_col + ch * 16, pk);
-        }
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = kf::ex2(x[2 * c] - m_use), p1 = kf::ex2(x[2 * c + 1] - m_use);
+        sum += p0 + p1;
+        pk[c] = kf::pack2<BF16>(p0, p1);
       }
-      l_sum += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
-      if (alternate) kf::mbar_arrive(&bars->turn[t ^ 1]);
+      l_sum += sum;
+      kf::tmem_st32(lane_base + s_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+      kf::tmem_st32(lane_base + s_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O row *= alpha (alpha == 1 on rows that keep their reference max)
         for (int c0 = 0; c0 < d_pad16; c0 += 32) {
