@@ -144,6 +144,14 @@ int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits
                       int64_t rows, int64_t D, void* o, float* lse, int dtype,
                       void* stream);
 
+/* ---- self-test of the bounded device wait -------------------------------
+ * No counterpart in the reference.  Launches one kernel that waits on a
+ * barrier nothing completes; after `budget_us` microseconds the wait gives
+ * up and writes KF_DEV_TIMEOUT into *status (device memory), the same path
+ * every attention kernel takes when a wait expires.  Used by the tests to
+ * show that an expired wait is reported and leaves the context usable. */
+int kf_selftest_bounded_wait(int32_t* status, int64_t budget_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

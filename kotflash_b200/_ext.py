@@ -67,6 +67,7 @@ SIGNATURES = {
     "kf_decode": (_I, [_T4, _T4, _T4, _T4, _T4, _I64, _T4, _VP, _I, _F, _I, _VP, _SZ, _VP]),
     "kf_merge_partials": (_I, [_VP, _VP, _I, _I64, _I64, _VP, _VP, _I, _VP]),
     "kf_decode_noalloc": (_I, [_T4, _T4, _T4, _T4, _T4, _I64, _T4, _VP, _I, _F, _I, _VP]),
+    "kf_selftest_bounded_wait": (_I, [_VP, _I64, _VP]),
 }
 
 _load_lock = threading.Lock()

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "kf_host.h"
+#include "kf_sm100.cuh"
 
 namespace kf {
 
@@ -113,3 +114,22 @@ int sm_count_current_device() {
 extern "C" int kf_version(void) { return 10000; }  // 1.0.0
 
 extern "C" const char* kf_last_error(void) { return kf::g_last_error.c_str(); }
+
+// Self-test of the bounded device wait: one thread waits on an mbarrier that
+// nothing arrives on, gives up after `budget_ns`, and records the timeout in
+// the status word, exactly as the attention kernels do when a peer stalls.
+static __global__ void selftest_wait_kernel(int32_t* status, uint64_t budget_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    kf::mbar_init(&bar, 1);
+    kf::fence_barrier_init();
+    kf::mbar_wait(&bar, 0, status, budget_ns);
+  }
+}
+
+extern "C" int kf_selftest_bounded_wait(int32_t* status, int64_t budget_us, void* stream) {
+  if (!status || budget_us <= 0 || budget_us > 10000000)
+    return kf::set_error(KF_ERR_INVALID, "kf_selftest_bounded_wait: need a status word and 0 < budget_us <= 1e7");
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, (uint64_t)budget_us * 1000u);
+  return kf::check_launch("kf_selftest_bounded_wait");
+}

@@ -75,14 +75,16 @@ KF_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on the phase with the given parity.  Returns false (and sets
-// *status) once the wall-time budget is spent, so no wait can run forever.
-KF_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+// *status to 1, the timeout code) once `budget_ns` of wall time is spent, so
+// no wait can run forever.
+KF_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status,
+                       uint64_t budget_ns = kWaitBudgetNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0 && global_timer_ns() - t0 > kWaitBudgetNs) {
+    if ((++spins & 255u) == 0 && global_timer_ns() - t0 > budget_ns) {
       if (status) atomicExch(status, 1);
       return false;
     }
