@@ -118,8 +118,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(sLD + kStages * 2 * kBM);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Heaviest first: every CTA of key block 0 (the most causal work) launches
+  // before any of key block 1, and so on, so the grid ends on light CTAs.
   const int bkv = blockIdx.x % (p.B * p.Hkv);
-  const int n = blockIdx.x / (p.B * p.Hkv);   // key block: all n = 0 CTAs launch first
+  const int n = blockIdx.x / (p.B * p.Hkv);
   const int b = bkv / p.Hkv, kvh = bkv % p.Hkv;
   const int i0 = p.causal ? min((n * kBN) / kBM, p.nqb) : 0;
   const int nq_steps = p.nqb - i0;

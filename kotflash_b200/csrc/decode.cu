@@ -318,52 +318,86 @@ struct MergeArgs {
   int64_t os0, os1, os2;
 };
 
+// One block of 128 threads merges the rows of a row group: first one warp per
+// row turns that row's S partial LSEs into normalised weights (kept in shared
+// memory), then each thread accumulates one 4-column chunk of one row over
+// all splits with independent, unrolled loads.
 template <bool BF16>
 __global__ void __launch_bounds__(128) merge_kernel(const MergeArgs a) {
+  extern __shared__ float wts[];  // [rows_per_block][S]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
-  if (row >= a.rows) return;
-  float mx = -INFINITY;
-  for (int s = lane; s < a.S; s += 32) mx = fmaxf(mx, a.part_lse[(int64_t)s * a.rows + row]);
+  const int tpr = a.D / 4;                  // threads per row
+  const int rpb = 128 / tpr;                // rows per block
+  const int64_t row0 = (int64_t)blockIdx.x * rpb;
+  __shared__ float row_lse[32];
+  for (int r = warp; r < rpb; r += 4) {
+    const int64_t row = row0 + r;
+    if (row >= a.rows) break;
+    float mx = -INFINITY;
+    for (int s = lane; s < a.S; s += 32) mx = fmaxf(mx, a.part_lse[(int64_t)s * a.rows + row]);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  float den = 0.f;
-  if (mx != -INFINITY) {
-    for (int s = lane; s < a.S; s += 32)
-      den += kf::ex2((a.part_lse[(int64_t)s * a.rows + row] - mx) * kLog2e);
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-  const float inv = den > 0.f ? 1.f / den : 0.f;
-  const int c4 = lane * 4;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (c4 < a.D && den > 0.f) {
-    for (int s = 0; s < a.S; ++s) {
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float den = 0.f;
+    for (int s = lane; s < a.S; s += 32) {
       const float ls = a.part_lse[(int64_t)s * a.rows + row];
-      if (ls == -INFINITY) continue;
-      const float w = kf::ex2((ls - mx) * kLog2e) * inv;
-      const float4 p = *reinterpret_cast<const float4*>(a.part_o + ((int64_t)s * a.rows + row) * a.D + c4);
-      acc[0] += w * p.x;
-      acc[1] += w * p.y;
-      acc[2] += w * p.z;
-      acc[3] += w * p.w;
+      const float w = (mx == -INFINITY || ls == -INFINITY) ? 0.f : kf::ex2((ls - mx) * kLog2e);
+      wts[r * a.S + s] = w;
+      den += w;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    for (int s = lane; s < a.S; s += 32) wts[r * a.S + s] *= inv;
+    if (lane == 0) row_lse[r] = den > 0.f ? mx + logf(den) : -INFINITY;
+  }
+  __syncthreads();
+  const int r = threadIdx.x / tpr, c4 = (threadIdx.x % tpr) * 4;
+  const int64_t row = row0 + r;
+  if (r >= rpb || row >= a.rows) return;
+  const float* wr = wts + r * a.S;
+  const float* src = a.part_o + row * a.D + c4;
+  const int64_t sstride = a.rows * a.D;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int s = 0;
+  for (; s + 8 <= a.S; s += 8) {
+    float4 p[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) p[u] = *reinterpret_cast<const float4*>(src + (int64_t)(s + u) * sstride);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float w = wr[s + u];
+      acc[0] += w * p[u].x;
+      acc[1] += w * p[u].y;
+      acc[2] += w * p[u].z;
+      acc[3] += w * p[u].w;
     }
   }
-  if (c4 < a.D) {
-    const int64_t bh = row / a.Sq;
-    const int64_t s_ = row % a.Sq;
-    const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
-    uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + c4;
-    const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
-    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+  for (; s < a.S; ++s) {
+    const float w = wr[s];
+    const float4 p = *reinterpret_cast<const float4*>(src + (int64_t)s * sstride);
+    acc[0] += w * p.x;
+    acc[1] += w * p.y;
+    acc[2] += w * p.z;
+    acc[3] += w * p.w;
   }
-  if (lane == 0 && a.lse) a.lse[row] = den > 0.f ? mx + logf(den) : -INFINITY;
+  const int64_t bh = row / a.Sq;
+  const int64_t s_ = row % a.Sq;
+  const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
+  uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + c4;
+  const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
+  *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+  if (c4 == 0 && a.lse) a.lse[row] = row_lse[r];
 }
 
 template <bool BF16>
 int launch_merge(const MergeArgs& m, cudaStream_t st) {
-  const unsigned blocks = (unsigned)((m.rows + 3) / 4);
-  merge_kernel<BF16><<<blocks, 128, 0, st>>>(m);
+  const int rpb = 128 / (m.D / 4);
+  const unsigned blocks = (unsigned)((m.rows + rpb - 1) / rpb);
+  const size_t smem = (size_t)rpb * m.S * sizeof(float);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(merge_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf merge: cannot reserve %zu bytes of shared memory", smem);
+  merge_kernel<BF16><<<blocks, 128, smem, st>>>(m);
   return kf::check_launch("kf merge");
 }
 
