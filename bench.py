@@ -372,8 +372,47 @@ def _append_at(cache, k, v, start):
     append_kv_cuda(cache.k, cache.v, k, v, start)
 
 
+def bench_odd_head_dim(peaks):
+    """B2 Hq16 Hkv4 S16384 fp16, D in {72, 96}, fwd+bwd, 1 GPU."""
+    from kotflash_b200.attention import attention_backward, attention_forward
+
+    res = []
+    b, hq, hkv, s = 2, 16, 4, 16384
+    for d in (72, 96):
+        g = torch.Generator(device="cuda").manual_seed(d)
+        q = torch.randn(b, hq, s, d, device="cuda", generator=g).half()
+        k = torch.randn(b, hkv, s, d, device="cuda", generator=g).half()
+        v = torch.randn(b, hkv, s, d, device="cuda", generator=g).half()
+        do = torch.randn(b, hq, s, d, device="cuda", generator=g).half()
+        for causal in (False, True):
+            scale = d ** -0.5
+            out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
+            attention_backward(q, k, v, out, lse, do, causal=causal, scale=scale)
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
+            ev[1].record()
+            attention_backward(q, k, v, out, lse, do, causal=causal, scale=scale)
+            ev[2].record()
+            torch.cuda.synchronize()
+            f = fwd_flops(b, hq, s, s, d, causal)
+            fm, bm = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+            tf = 3.5 * f / ((fm + bm) * 1e-3) / 1e12
+            res.append({"d": d, "causal": causal, "fwd_ms": round(fm, 3), "bwd_ms": round(bm, 3),
+                        "fwd_bwd_tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 3)})
+        del q, k, v, do
+        torch.cuda.empty_cache()
+    return res
+
+
 def bench_decode_multi_gpu(world, rank):
-    """cfg3 at Sk=131072, KV split across ranks; compute and exchange timed apart."""
+    """cfg3 at Sk=131072 with the KV sequence split across ranks.
+
+    Each rank's sequence (split-KV decode of its chunk, pack, NCCL all-gather,
+    LSE merge) is captured in a CUDA graph and replayed; the compute-only part
+    is captured separately so compute and exchange are reported apart.  Max
+    over ranks of device time per call."""
     from kotflash_b200 import distributed as kd
     from kotflash_b200.attention import _decode_forward
 
@@ -387,34 +426,39 @@ def bench_decode_multi_gpu(world, rank):
         q = torch.randn(2, 8, sq, 64, device="cuda", generator=g).half()
         kl, vl = k_full[:, :, lo:hi].contiguous(), v_full[:, :, lo:hi].contiguous()
         del k_full, v_full
-        for _ in range(5):
+
+        def full(_i):
             kd.decode_kv_split(q, kl, vl, scale=0.125)
+
+        def local(_i):
+            _decode_forward(q, kl, vl, scale=0.125, want_lse=True)
+
+        barrier(world)
+        t_all = _graph_time(full, 8, replays=5)
+        barrier(world)
+        t_c = _graph_time(local, 8, replays=5)
+        a = max_over_ranks(t_all, world)
+        c = max_over_ranks(t_c, world)
+        out.append({"sq": sq, "sk": sk, "ranks": world, "keys_per_rank": hi - lo,
+                    "compute_us": round(c * 1e3, 2), "exchange_merge_us": round((a - c) * 1e3, 2),
+                    "total_us": round(a * 1e3, 2), "us_per_token": round(a * 1e3 / sq, 3),
+                    "timing": "CUDA-graph replay, max over ranks"})
         torch.cuda.synchronize()
-        t_c, t_x, t_all = [], [], []
-        for _ in range(20):
-            e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-            barrier(world)
-            e[0].record()
-            o, lse = _decode_forward(q, kl, vl, scale=0.125, want_lse=True)
-            e[1].record()
-            po, pl = kd.gather_partials(kd.pack_partial(o, lse))
-            e[2].record()
-            kd.merge_partials(po, pl, tuple(q.shape), q.dtype)
-            e[3].record()
-            torch.cuda.synchronize()
-            t_c.append(e[0].elapsed_time(e[1]))
-            t_x.append(e[1].elapsed_time(e[2]))
-            t_all.append(e[0].elapsed_time(e[3]))
-        c = max_over_ranks(statistics.median(t_c), world)
-        x = max_over_ranks(statistics.median(t_x), world)
-        a = max_over_ranks(statistics.median(t_all), world)
-        out.append({"sq": sq, "sk": sk, "ranks": world, "compute_us": round(c * 1e3, 2),
-                    "allgather_us": round(x * 1e3, 2), "total_us": round(a * 1e3, 2),
-                    "us_per_token": round(a * 1e3 / sq, 3)})
     return out
 
 
 # --------------------------------------------------------------------------- CPU baseline
+def use_all_host_cores() -> int:
+    """Let the CPU baseline use every core this process may run on (torchrun sets
+    OMP_NUM_THREADS=1 for its workers; rank 0 runs the CPU legs alone)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
 def cpu_unit_sample(dtype_name: str, budget_s: float = 12.0, min_runs: int = 1):
     """Time the reference CPU route on (batch, KV-head) units of the prefill config.
 
@@ -453,6 +497,7 @@ def run_reference(args, world, rank):
     """--impl reference: the reference's CPU route on the host cores (rank 0 only)."""
     if rank != 0:
         return 0
+    use_all_host_cores()
     g = torch.Generator().manual_seed(0)
     from oracle import attention_oracle as oracle
 
@@ -595,9 +640,11 @@ def main(argv=None) -> int:
             multi = bench_decode_multi_gpu(world, rank)
         elif rank == 0:
             decode = {"sweep": bench_decode_sweep(peaks), "kv_cache_loop": bench_cache_loop(peaks)}
+    odd = bench_odd_head_dim(peaks) if (rank == 0 and world == 1 and not args.no_decode) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
+        use_all_host_cores()
         tflops, per_unit, dtn, runs, threads = cpu_unit_sample(args.dtype)
         cpu = {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                "sample": f"{runs} run(s) of one (batch, kv-head) unit of 32 ({dtn}): reference "
@@ -619,6 +666,7 @@ def main(argv=None) -> int:
             "gpu_launches": 4 * args.steps,
             "cpu_baseline": cpu,
             "decode": decode, "decode_multi_gpu": multi,
+            "odd_head_dim_training": odd,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
