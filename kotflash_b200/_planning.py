@@ -6,7 +6,7 @@ Replaces the reference's ``kotflash/_planning.py``.  The helpers ``cdiv``,
 contracts (``_planning.py:11-46``).  ``split_kv_plan`` keeps the reference's
 partition invariant (splits cover ``[0, Sk)`` with no gap and no empty split,
 ``tests/test_planning.py:66-79``) but is sized for a 148-SM B200 instead of a
-40-SM T4: the split count fills about two waves of CTAs, where one CTA works
+40-SM T4: the split count fills about two CTAs per SM, where one CTA works
 on one (split, batch, KV head) with every query row of the GQA group packed
 together.  The reference's T4 exact-shape routing tables
 (``_planning.py:49-76``) have no counterpart here.

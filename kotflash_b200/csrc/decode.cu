@@ -52,6 +52,7 @@ struct DecodeArgs {
   int rows;  // G * Sq packed rows per KV head
   int64_t prow_total;  // B * Hq * Sq
   float scale_log2;
+  int32_t* status;     // device word set when a bounded wait expires (may be null)
 };
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
@@ -64,15 +65,33 @@ __device__ __forceinline__ float warp_max4(float x) {
   return x;
 }
 
-template <bool BF16, int DP, int MT, int STAGES>
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs a) {
+// Shared-memory address of 16-byte chunk `c` of row `r` in a TMA tile stored
+// as 64-column panels of `rows` x 128 B with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t tma_swz(int r, int c, int rows) {
+  return (uint32_t)((c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+constexpr int kTileN = kWarps * kTileKeys;  // 64 keys per TMA tile
+
+// NP = 64-column panels of the padded head dim (1 or 2), MT = 16-row m-tiles of
+// packed query rows, STAGES = depth of the K/V ring.
+template <bool BF16, int NP, int MT, int STAGES>
+__global__ void __launch_bounds__(kThreads)
+decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                    const DecodeArgs a) {
+  constexpr int DP = NP * 64;
   constexpr int ROWS = MT * 16;
-  constexpr int ROW_BYTES = DP * 2;
-  constexpr int CHUNKS = DP / 8;  // 16-byte chunks per row
-  constexpr int TILE_BYTES = kTileKeys * ROW_BYTES;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sQ = smem;
-  uint8_t* sKV = smem + ROWS * ROW_BYTES;  // [warp][stage][K|V][16][DP]
+  constexpr int Q_ROW_BYTES = DP * 2;
+  constexpr int CHUNKS = DP / 8;                 // 16-byte chunks per row
+  constexpr int PANEL = kTileN * 128;            // one 64-column panel of a tile
+  constexpr int TILE = NP * PANEL;               // K (or V) tile bytes
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sKV = smem;                           // [stage][K tile | V tile]
+  uint8_t* sQ = smem + STAGES * 2 * TILE;        // [ROWS][DP] (row-local XOR swizzle)
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
+  __shared__ int abort_any;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x;
@@ -80,11 +99,41 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
   const int row0 = blockIdx.z * ROWS;
   const int key_begin = split * a.chunk;
   const int key_end = min(key_begin + a.chunk, a.Sk);
+  const int n_tiles = (key_end - key_begin + kTileN - 1) / kTileN;
   const bool fused = a.nk != nullptr;
 
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      kf::mbar_init(&full[s], 1);
+      kf::mbar_init(&empty[s], kWarps);
+    }
+    kf::fence_barrier_init();
+    abort_any = 0;
+  }
+  __syncthreads();
+  int issued = 0;  // tiles whose loads thread 0 has issued
+  // one thread streams K/V tiles (TMA, no multicast); the ring is recycled
+  // once all four warps have released a stage
+  auto issue = [&](int t) {
+    const int s = t % STAGES;
+    uint8_t* kt = sKV + s * 2 * TILE;
+    kf::mbar_arrive_expect_tx(&full[s], 2 * TILE);
+#pragma unroll
+    for (int pn = 0; pn < NP; ++pn) {
+      kf::tma_load_4d(kt + pn * PANEL, &map_k, &full[s], pn * 64, key_begin + t * kTileN, kvh, b);
+      kf::tma_load_4d(kt + TILE + pn * PANEL, &map_v, &full[s], pn * 64, key_begin + t * kTileN, kvh, b);
+    }
+  };
+  if (tid == 0) {
+    kf::tma_prefetch_desc(&map_k);
+    kf::tma_prefetch_desc(&map_v);
+    for (int t = 0; t < STAGES && t < n_tiles; ++t) issue(t);
+    issued = min(STAGES, n_tiles);
+  }
+
   // fused append: the CTA of the split owning the new position (row block 0)
-  // writes the new K/V row into the cache; every CTA reads it from nk/nv.
-  if (fused && blockIdx.z == 0 && a.past_len >= key_begin && a.past_len < key_end && warp == 0) {
+  // writes the new K/V row into the cache; every CTA substitutes it in smem.
+  if (fused && blockIdx.z == 0 && a.past_len >= key_begin && a.past_len < key_end && warp == 1) {
     for (int c = lane; c < a.D / 8; c += 32) {
       const uint4 kv = *reinterpret_cast<const uint4*>(a.nk + b * a.nks[0] + kvh * a.nks[1] + c * 8);
       const uint4 vv = *reinterpret_cast<const uint4*>(a.nv + b * a.nvs[0] + kvh * a.nvs[1] + c * 8);
@@ -100,41 +149,11 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
     const bool ok = pr < a.rows && c * 8 < a.D;
     const int g = ok ? pr / a.Sq : 0, s = ok ? pr % a.Sq : 0;
     const uint16_t* src = a.q + b * a.qs[0] + (int64_t)(kvh * a.G + g) * a.qs[1] + s * a.qs[2] + (ok ? c * 8 : 0);
-    kf::cp_async16(sQ + swz(r, c, ROW_BYTES), src, ok);
+    kf::cp_async16(sQ + swz(r, c, Q_ROW_BYTES), src, ok);
   }
   kf::cp_async_commit();
   kf::cp_async_wait<0>();
   __syncthreads();
-
-  // ---- per-warp pipeline over 16-key tiles j = warp, warp+4, ...
-  const int n_tiles = (key_end - key_begin + kTileKeys - 1) / kTileKeys;
-  const int n_my = n_tiles > warp ? (n_tiles - warp + kWarps - 1) / kWarps : 0;
-  uint8_t* my_ring = sKV + warp * STAGES * 2 * TILE_BYTES;
-  const uint16_t* kbase = a.k + b * a.ks[0] + kvh * a.ks[1];
-  const uint16_t* vbase = a.v + b * a.vs[0] + kvh * a.vs[1];
-
-  auto load_tile = [&](int it, int stage) {
-    const int key0 = key_begin + (warp + it * kWarps) * kTileKeys;
-    uint8_t* sk = my_ring + stage * 2 * TILE_BYTES;
-    uint8_t* sv = sk + TILE_BYTES;
-#pragma unroll
-    for (int i = lane; i < kTileKeys * CHUNKS; i += 32) {
-      const int r = i / CHUNKS, c = i % CHUNKS;
-      const int key = key0 + r;
-      const bool ok = key < key_end && c * 8 < a.D;
-      const uint16_t* ks;
-      const uint16_t* vs;
-      if (fused && key == a.past_len) {
-        ks = a.nk + b * a.nks[0] + kvh * a.nks[1];
-        vs = a.nv + b * a.nvs[0] + kvh * a.nvs[1];
-      } else {
-        ks = kbase + (int64_t)(ok ? key : key_begin) * a.ks[2];
-        vs = vbase + (int64_t)(ok ? key : key_begin) * a.vs[2];
-      }
-      kf::cp_async16(sk + swz(r, c, ROW_BYTES), ks + (ok ? c * 8 : 0), ok);
-      kf::cp_async16(sv + swz(r, c, ROW_BYTES), vs + (ok ? c * 8 : 0), ok);
-    }
-  };
 
   float m_run[MT][2], l_run[MT][2];
   float o_acc[MT][DP / 8][4];
@@ -145,23 +164,47 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
 #pragma unroll
     for (int n = 0; n < DP / 8; ++n) o_acc[mt][n][0] = o_acc[mt][n][1] = o_acc[mt][n][2] = o_acc[mt][n][3] = 0.f;
   }
-
-#pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < n_my) load_tile(s, s);
-    kf::cp_async_commit();
-  }
   const uint32_t sQ_u = kf::smem_u32(sQ);
-  for (int it = 0; it < n_my; ++it) {
-    if (it + STAGES - 1 < n_my) load_tile(it + STAGES - 1, (it + STAGES - 1) % STAGES);
-    kf::cp_async_commit();
-    kf::cp_async_wait<STAGES - 1>();
-    __syncwarp();
-    const uint32_t sk_u = kf::smem_u32(my_ring + (it % STAGES) * 2 * TILE_BYTES);
-    const uint32_t sv_u = sk_u + TILE_BYTES;
-    const int key0 = key_begin + (warp + it * kWarps) * kTileKeys;
+  const int wr0 = warp * kTileKeys;   // this warp's 16 rows of every tile
+  bool ok = true;
+  int t_stop = n_tiles;
+  for (int t = 0; t < n_tiles; ++t) {
+    const int st = t % STAGES;
+    const uint32_t ph = (t / STAGES) & 1;
+    // thread 0 refills the stage freed by the previous tile once all warps left it
+    if (tid == 0 && t > 0 && t - 1 + STAGES < n_tiles) {
+      const int sp = (t - 1) % STAGES;
+      if (kf::mbar_wait(&empty[sp], ((t - 1) / STAGES) & 1, a.status)) {
+        issue(t - 1 + STAGES);
+        issued = t + STAGES;
+      } else {
+        abort_any = 1;
+      }
+    }
+    // warp-uniform outcome: no lane reaches the collective ldmatrix/mma alone
+    ok = __all_sync(0xffffffffu, kf::mbar_wait(&full[st], ph, a.status) && !*(volatile int*)&abort_any);
+    if (!ok) {
+      t_stop = t;
+      if (lane == 0) abort_any = 1;
+      break;
+    }
+    uint8_t* kt = sKV + st * 2 * TILE;
+    uint8_t* vt = kt + TILE;
+    const int key0 = key_begin + t * kTileN + wr0;
+    if (fused && a.past_len >= key0 && a.past_len < key0 + kTileKeys) {
+      const int r = wr0 + (int)(a.past_len - key0);
+      for (int c = lane; c < CHUNKS; c += 32) {
+        const bool in = c * 8 < a.D;
+        const uint4 kv = in ? *reinterpret_cast<const uint4*>(a.nk + b * a.nks[0] + kvh * a.nks[1] + c * 8) : make_uint4(0, 0, 0, 0);
+        const uint4 vv = in ? *reinterpret_cast<const uint4*>(a.nv + b * a.nvs[0] + kvh * a.nvs[1] + c * 8) : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(kt + tma_swz(r, c, kTileN)) = kv;
+        *reinterpret_cast<uint4*>(vt + tma_swz(r, c, kTileN)) = vv;
+      }
+      __syncwarp();
+    }
+    const uint32_t sk_u = kf::smem_u32(kt), sv_u = kf::smem_u32(vt);
 
-    // S = Q K^T for 16 keys
+    // S = Q K^T for this warp's 16 keys
     float sc[MT][2][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -170,11 +213,11 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
 #pragma unroll
     for (int kk = 0; kk < DP / 16; ++kk) {
       uint32_t kb[4];
-      kf::ldmatrix_x4(kb, sk_u + swz((lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), ROW_BYTES));
+      kf::ldmatrix_x4(kb, sk_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), kTileN));
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         uint32_t qa[4];
-        kf::ldmatrix_x4(qa, sQ_u + swz(mt * 16 + (lane & 15), 2 * kk + (lane >> 4), ROW_BYTES));
+        kf::ldmatrix_x4(qa, sQ_u + swz(mt * 16 + (lane & 15), 2 * kk + (lane >> 4), Q_ROW_BYTES));
         kf::mma_16816<BF16>(sc[mt][0], qa, kb[0], kb[1]);
         kf::mma_16816<BF16>(sc[mt][1], qa, kb[2], kb[3]);
       }
@@ -203,27 +246,29 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
         for (int j = 0; j < 4; ++j) p[j] = kf::ex2(x[j] - m_use);
         l_run[mt][half] = l_run[mt][half] * alpha + (p[0] + p[1] + p[2] + p[3]);
         m_run[mt][half] = m_new;
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // skip when no row max moved
 #pragma unroll
-        for (int n = 0; n < DP / 8; ++n) {
-          o_acc[mt][n][half * 2 + 0] *= alpha;
-          o_acc[mt][n][half * 2 + 1] *= alpha;
+          for (int n = 0; n < DP / 8; ++n) {
+            o_acc[mt][n][half * 2 + 0] *= alpha;
+            o_acc[mt][n][half * 2 + 1] *= alpha;
+          }
         }
-        pa[half] = kf::pack2<BF16>(p[0], p[1]);      // keys 0-7 of the tile
+        pa[half] = kf::pack2<BF16>(p[0], p[1]);      // keys 0-7 of the warp's 16
         pa[2 + half] = kf::pack2<BF16>(p[2], p[3]);  // keys 8-15
       }
 #pragma unroll
       for (int dn = 0; dn < DP / 16; ++dn) {
         uint32_t vb[4];
-        kf::ldmatrix_x4_trans(vb, sv_u + swz(lane & 15, 2 * dn + (lane >> 4), ROW_BYTES));
+        kf::ldmatrix_x4_trans(vb, sv_u + tma_swz(wr0 + (lane & 15), 2 * dn + (lane >> 4), kTileN));
         kf::mma_16816<BF16>(o_acc[mt][2 * dn], pa, vb[0], vb[1]);
         kf::mma_16816<BF16>(o_acc[mt][2 * dn + 1], pa, vb[2], vb[3]);
       }
     }
     __syncwarp();
+    if (lane == 0) kf::mbar_arrive(&empty[st]);
   }
-  kf::cp_async_wait<0>();
 
-  // ---- merge the 4 warps in shared memory (reuses the pipeline buffers)
+  // ---- merge the 4 warps in shared memory (reuses the ring: all tiles consumed)
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -234,6 +279,25 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
       l_run[mt][half] = l;
     }
   __syncthreads();
+  if (abort_any) {
+    // a bounded wait expired: let the loads already in flight land (bounded),
+    // then make the failure visible as NaN outputs instead of stale data
+    if (tid == 0)
+      for (int t2 = t_stop; t2 < issued; ++t2)
+        kf::mbar_wait(&full[t2 % STAGES], (t2 / STAGES) & 1, nullptr, 100000000ull);
+    const int valid = min(ROWS, a.rows - row0);
+    const int64_t pbase = (int64_t)(b * a.Hkv + kvh) * a.rows + row0;
+    for (int i = tid; i < valid * a.D; i += kThreads) {
+      const int r = i / a.D, c = i % a.D, pr = row0 + r;
+      if (a.num_splits == 1) {
+        a.o[b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2] + c] = 0x7fffu;
+      } else {
+        a.part_o[((int64_t)split * a.prow_total + pbase + r) * a.D + c] = __int_as_float(0x7fc00000);
+        if (c == 0) a.part_lse[(int64_t)split * a.prow_total + pbase + r] = 0.f;
+      }
+    }
+    return;
+  }
   float* ml = reinterpret_cast<float*>(smem);          // [warp][ROWS][2]
   float* row_w = ml + kWarps * ROWS * 2;               // [warp][ROWS] weights
   float* row_lse = row_w + kWarps * ROWS;              // [ROWS]
@@ -318,21 +382,20 @@ struct MergeArgs {
   int64_t os0, os1, os2;
 };
 
-// One block of 128 threads merges the rows of a row group: first one warp per
-// row turns that row's S partial LSEs into normalised weights (kept in shared
-// memory), then each thread accumulates one 4-column chunk of one row over
-// all splits with independent, unrolled loads.
+// One 128-thread block per output row.  Warp 0 turns the row's S partial LSEs
+// into normalised weights in shared memory; then thread (chunk c, group g)
+// accumulates 4 columns over splits g, g + G, g + 2G, ... (G = 128 / (D/4)
+// groups), all loads independent, and the G partial sums are reduced through
+// shared memory.  Few dependent rounds even with hundreds of splits.
 template <bool BF16>
 __global__ void __launch_bounds__(128) merge_kernel(const MergeArgs a) {
-  extern __shared__ float wts[];  // [rows_per_block][S]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tpr = a.D / 4;                  // threads per row
-  const int rpb = 128 / tpr;                // rows per block
-  const int64_t row0 = (int64_t)blockIdx.x * rpb;
-  __shared__ float row_lse[32];
-  for (int r = warp; r < rpb; r += 4) {
-    const int64_t row = row0 + r;
-    if (row >= a.rows) break;
+  extern __shared__ float sm[];          // [S] weights, then [G][D] partial sums
+  float* wts = sm;
+  float* part = sm + ((a.S + 3) & ~3);
+  __shared__ float row_lse;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t row = blockIdx.x;
+  if (tid < 32) {
     float mx = -INFINITY;
     for (int s = lane; s < a.S; s += 32) mx = fmaxf(mx, a.part_lse[(int64_t)s * a.rows + row]);
 #pragma unroll
@@ -341,98 +404,118 @@ __global__ void __launch_bounds__(128) merge_kernel(const MergeArgs a) {
     for (int s = lane; s < a.S; s += 32) {
       const float ls = a.part_lse[(int64_t)s * a.rows + row];
       const float w = (mx == -INFINITY || ls == -INFINITY) ? 0.f : kf::ex2((ls - mx) * kLog2e);
-      wts[r * a.S + s] = w;
+      wts[s] = w;
       den += w;
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
     const float inv = den > 0.f ? 1.f / den : 0.f;
-    for (int s = lane; s < a.S; s += 32) wts[r * a.S + s] *= inv;
-    if (lane == 0) row_lse[r] = den > 0.f ? mx + logf(den) : -INFINITY;
+    __syncwarp();
+    for (int s = lane; s < a.S; s += 32) wts[s] *= inv;
+    if (lane == 0) row_lse = den > 0.f ? mx + logf(den) : -INFINITY;
   }
   __syncthreads();
-  const int r = threadIdx.x / tpr, c4 = (threadIdx.x % tpr) * 4;
-  const int64_t row = row0 + r;
-  if (r >= rpb || row >= a.rows) return;
-  const float* wr = wts + r * a.S;
-  const float* src = a.part_o + row * a.D + c4;
-  const int64_t sstride = a.rows * a.D;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int s = 0;
-  for (; s + 8 <= a.S; s += 8) {
-    float4 p[8];
+  const int tpr = a.D / 4;               // threads per split (one 4-column chunk each)
+  const int groups = 128 / tpr;
+  const int c = tid % tpr, g = tid / tpr;
+  if (g < groups) {
+    const float* src = a.part_o + row * a.D + c * 4;
+    const int64_t sstride = a.rows * a.D;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int s = g;
+    for (; s + 3 * groups < a.S; s += 4 * groups) {
+      float4 p[4];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) p[u] = *reinterpret_cast<const float4*>(src + (int64_t)(s + u) * sstride);
+      for (int u = 0; u < 4; ++u) p[u] = *reinterpret_cast<const float4*>(src + (int64_t)(s + u * groups) * sstride);
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float w = wr[s + u];
-      acc[0] += w * p[u].x;
-      acc[1] += w * p[u].y;
-      acc[2] += w * p[u].z;
-      acc[3] += w * p[u].w;
+      for (int u = 0; u < 4; ++u) {
+        const float w = wts[s + u * groups];
+        acc[0] += w * p[u].x;
+        acc[1] += w * p[u].y;
+        acc[2] += w * p[u].z;
+        acc[3] += w * p[u].w;
+      }
     }
+    for (; s < a.S; s += groups) {
+      const float w = wts[s];
+      const float4 p = *reinterpret_cast<const float4*>(src + (int64_t)s * sstride);
+      acc[0] += w * p.x;
+      acc[1] += w * p.y;
+      acc[2] += w * p.z;
+      acc[3] += w * p.w;
+    }
+    *reinterpret_cast<float4*>(part + g * a.D + c * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
-  for (; s < a.S; ++s) {
-    const float w = wr[s];
-    const float4 p = *reinterpret_cast<const float4*>(src + (int64_t)s * sstride);
-    acc[0] += w * p.x;
-    acc[1] += w * p.y;
-    acc[2] += w * p.z;
-    acc[3] += w * p.w;
+  __syncthreads();
+  if (tid < tpr) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int gg = 0; gg < groups; ++gg) {
+      const float4 p = *reinterpret_cast<const float4*>(part + gg * a.D + tid * 4);
+      acc[0] += p.x;
+      acc[1] += p.y;
+      acc[2] += p.z;
+      acc[3] += p.w;
+    }
+    const int64_t bh = row / a.Sq;
+    const int64_t s_ = row % a.Sq;
+    const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
+    uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + tid * 4;
+    const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+    if (tid == 0 && a.lse) a.lse[row] = row_lse;
   }
-  const int64_t bh = row / a.Sq;
-  const int64_t s_ = row % a.Sq;
-  const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
-  uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + c4;
-  const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
-  *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-  if (c4 == 0 && a.lse) a.lse[row] = row_lse[r];
 }
 
 template <bool BF16>
 int launch_merge(const MergeArgs& m, cudaStream_t st) {
-  const int rpb = 128 / (m.D / 4);
-  const unsigned blocks = (unsigned)((m.rows + rpb - 1) / rpb);
-  const size_t smem = (size_t)rpb * m.S * sizeof(float);
+  const int groups = 128 / (m.D / 4);
+  const size_t smem = (size_t)(((m.S + 3) & ~3) + groups * m.D) * sizeof(float);
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(merge_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf merge: cannot reserve %zu bytes of shared memory", smem);
-  merge_kernel<BF16><<<blocks, 128, smem, st>>>(m);
+  if (m.rows > 0x7fffffffLL) return kf::set_error(KF_ERR_UNSUPPORTED, "kf merge: too many rows");
+  merge_kernel<BF16><<<(unsigned)m.rows, 128, smem, st>>>(m);
   return kf::check_launch("kf merge");
 }
 
-template <bool BF16, int DP, int MT>
-int launch_split(const DecodeArgs& a, int row_blocks, cudaStream_t st) {
-  constexpr int STAGES = DP == 64 ? 4 : 3;
+template <bool BF16, int NP, int MT>
+int launch_split(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int row_blocks,
+                 cudaStream_t st) {
+  constexpr int STAGES = NP == 1 ? 4 : 2;
+  constexpr int DP = NP * 64;
   constexpr int ROWS = MT * 16;
-  const size_t pipe = (size_t)ROWS * DP * 2 + (size_t)kWarps * STAGES * 2 * kTileKeys * DP * 2;
-  const size_t merge = (size_t)kWarps * ROWS * 3 * 4 + ROWS * 4 + (size_t)kWarps * ROWS * DP * 4;
+  const size_t pipe = 1024 + (size_t)STAGES * 2 * NP * kTileN * 128 + (size_t)ROWS * DP * 2;
+  const size_t merge = 1024 + (size_t)kWarps * ROWS * 3 * 4 + ROWS * 4 + (size_t)kWarps * ROWS * DP * 4;
   const size_t smem = pipe > merge ? pipe : merge;
-  auto kern = decode_split_kernel<BF16, DP, MT, STAGES>;
+  auto kern = decode_split_kernel<BF16, NP, MT, STAGES>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
   dim3 grid(a.num_splits, a.B * a.Hkv, row_blocks);
-  kern<<<grid, kThreads, smem, st>>>(a);
+  kern<<<grid, kThreads, smem, st>>>(mk, mv, a);
   return kf::check_launch("kf_decode");
 }
 
 template <bool BF16>
-int dispatch_split(const DecodeArgs& a, cudaStream_t st) {
-  const int dp = a.D <= 64 ? 64 : 128;
-  const int mt_max = dp == 64 ? 4 : 2;
+int dispatch_split(const DecodeArgs& a, const kf_tensor4* k, const kf_tensor4* v, cudaStream_t st) {
+  CUtensorMap mk, mv;
+  int rc;
+  if ((rc = kf::encode_tmap_4d(&mk, k, 64, kTileN))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mv, v, 64, kTileN))) return rc;
+  const int np = a.D <= 64 ? 1 : 2;
+  const int mt_max = np == 1 ? 4 : 2;
   int mt = (a.rows + 15) / 16;
   if (mt > mt_max) mt = mt_max;
   const int row_blocks = (a.rows + mt * 16 - 1) / (mt * 16);
-  if (dp == 64) {
+  if (np == 1) {
     switch (mt) {
-      case 1: return launch_split<BF16, 64, 1>(a, row_blocks, st);
-      case 2: return launch_split<BF16, 64, 2>(a, row_blocks, st);
-      case 3: return launch_split<BF16, 64, 3>(a, row_blocks, st);
-      default: return launch_split<BF16, 64, 4>(a, row_blocks, st);
+      case 1: return launch_split<BF16, 1, 1>(a, mk, mv, row_blocks, st);
+      case 2: return launch_split<BF16, 1, 2>(a, mk, mv, row_blocks, st);
+      case 3: return launch_split<BF16, 1, 3>(a, mk, mv, row_blocks, st);
+      default: return launch_split<BF16, 1, 4>(a, mk, mv, row_blocks, st);
     }
   }
-  if (mt == 1) return launch_split<BF16, 128, 1>(a, row_blocks, st);
-  return launch_split<BF16, 128, 2>(a, row_blocks, st);
+  if (mt == 1) return launch_split<BF16, 2, 1>(a, mk, mv, row_blocks, st);
+  return launch_split<BF16, 2, 2>(a, mk, mv, row_blocks, st);
 }
 
 bool rows16(const kf_tensor4* t) {
@@ -548,6 +631,7 @@ extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tens
   a.scale_log2 = scale * kLog2e;
   a.part_o = nullptr;
   a.part_lse = nullptr;
+  a.status = nullptr;
   if (num_splits > 1) {
     const size_t need = kf_decode_workspace_bytes(B, Hq, Sq, D, num_splits);
     if (!workspace || workspace_bytes < need)
@@ -559,7 +643,7 @@ extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tens
   if (a.G * a.Sq > (1 << 20)) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many rows per KV head");
   if ((int64_t)B * Hkv > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: B*Hkv too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int rc = dtype == KF_BF16 ? dispatch_split<true>(a, st) : dispatch_split<false>(a, st);
+  int rc = dtype == KF_BF16 ? dispatch_split<true>(a, k, v, st) : dispatch_split<false>(a, k, v, st);
   if (rc != KF_OK || num_splits == 1) return rc;
   MergeArgs m;
   m.part_o = a.part_o;
