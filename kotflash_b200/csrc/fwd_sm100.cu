@@ -12,17 +12,25 @@
 //   warps 0-3  softmax for tile 0   (thread t owns query row t = TMEM lane t)
 //   warps 4-7  softmax for tile 1
 //   warp  8    TMA producer (Q once, then K/V blocks of 128 keys)
-//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+//   warp  9    TMEM allocator + tcgen05.mma issuer for tile 0
+//   warp 10    tcgen05.mma issuer for tile 1
 // Tensor memory (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P (16-bit) overwrites the first 64 columns of its S tile and feeds the
 // PV product directly from TMEM (A operand in tensor memory).
-// The MMA issue order per KV block j is
-//   O0 += P0_j V_j ; S0 = Q0 K_{j+1}^T ; O1 += P1_j V_j ; S1 = Q1 K_{j+1}^T
-// so one tile's softmax overlaps the other tile's two GEMMs.  A tile's
-// "S ready" commit also covers its previous PV, which makes O safe to rescale
-// when the softmax sees the next S.  The running max is only raised (and O
-// rescaled) when it grows by more than 2^8, so most blocks skip the O
-// round trip; P stays <= 256, which fp16/bf16 hold exactly enough.
+// Each tile's issuer runs, per KV block j,
+//   O_t += P_t,j V_j ; S_t = Q_t K_{j+1}^T
+// so one tile's softmax overlaps the other tile's two GEMMs.  Two issuing
+// threads matter on sm_100: the tensor pipe holds almost no queued MMAs, so
+// every cycle an issuing thread spends on an mbarrier wait, a tcgen05 fence
+// or a commit would idle the pipe; with one issuer per tile, the other tile's
+// MMAs fill those gaps.  A tile's "S ready" commit also covers its previous
+// PV, which makes O safe to rescale when the softmax sees the next S.  The
+// running max is only raised (and O rescaled) when it grows by more than 2^8,
+// so most blocks skip the O round trip; P stays <= 256, which fp16/bf16 hold
+// exactly enough.  The softmax computes its exponentials partly on the MUFU
+// unit and partly as a polynomial on the fp32 pipe (packed f32x2 arithmetic),
+// because 16 MUFU results per clock per SM alone cannot keep up with the
+// tensor cores at head_dim 128.
 #include <math.h>
 
 #include "kf_host.h"
@@ -32,11 +40,14 @@ namespace {
 
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kStages = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Of every 8 exponential pairs in an unmasked block, this many run as the
+// fp32-pipe polynomial and the rest on MUFU.
+constexpr int kPolyPairs = 2;
 
 struct FwdParams {
   uint16_t* o;
@@ -56,7 +67,8 @@ struct __align__(8) FwdBarriers {
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[2], p_full[2];
-  uint64_t o_final;
+  uint64_t o_final[2];
+  uint64_t turn[2];  // exponential phases of the two tiles alternate
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -130,19 +142,21 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   const int nblk = ti.n_blocks;
   constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
 
+  const int nt = ti.valid[1] ? 2 : 1;  // Q tiles in use == MMA issuers
   if (tid == 0) {
     kf::mbar_init(&bars->q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       kf::mbar_init(&bars->k_full[s], 1);
-      kf::mbar_init(&bars->k_empty[s], 1);
+      kf::mbar_init(&bars->k_empty[s], nt);  // one commit per issuer
       kf::mbar_init(&bars->v_full[s], 1);
-      kf::mbar_init(&bars->v_empty[s], 1);
+      kf::mbar_init(&bars->v_empty[s], nt);
     }
     for (int t = 0; t < 2; ++t) {
       kf::mbar_init(&bars->s_full[t], 1);
       kf::mbar_init(&bars->p_full[t], 128);
+      kf::mbar_init(&bars->o_final[t], 1);
+      kf::mbar_init(&bars->turn[t], 128);
     }
-    kf::mbar_init(&bars->o_final, 1);
     bars->abort_flag = 0;
     kf::fence_barrier_init();
   }
@@ -163,9 +177,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int nq = ti.valid[1] ? 2 : 1;
-      kf::mbar_arrive_expect_tx(&bars->q_full, nq * TILE);
-      for (int t = 0; t < nq; ++t)
+      kf::mbar_arrive_expect_tx(&bars->q_full, nt * TILE);
+      for (int t = 0; t < nt; ++t)
         for (int pn = 0; pn < NP; ++pn)
           kf::tma_load_4d(sQ + t * TILE + pn * PANEL, &map_q, &bars->q_full, pn * 64, ti.row0[t],
                           ti.head[t], ti.b);
@@ -184,40 +197,40 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
                           j * kBlockN, ti.kvh, ti.b);
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers
+    const int t = warp - 9;  // this thread issues every MMA of Q tile t
+    if (lane == 0 && t < nt) {
       const uint32_t idesc_qk = kf::make_idesc_f16(BF16, kBlockM, kBlockN, 0, 0);
       const uint32_t idesc_pv = kf::make_idesc_f16(BF16, kBlockM, d_pad16, 0, 1);
-      const uint32_t sq_u = kf::smem_u32(sQ), sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
-      const int nt = ti.valid[1] ? 2 : 1;
-      // Each GEMM is one straight-line run of MMAs (compile-time trip counts):
-      // branches between consecutive tcgen05.mma slow their issue down.
-      auto issue_qk = [&](int t, int j) {
-        const uint32_t qb = sq_u + t * TILE, kb = sk_u + (j % kStages) * TILE;
+      // Descriptors are built once; each MMA only adds a compile-time offset
+      // to the low word of a base descriptor.
+      const kf::SDesc dq = kf::make_sdesc_split(kf::smem_u32(sQ + t * TILE), 16, 1024);
+      const kf::SDesc dk = kf::make_sdesc_split(kf::smem_u32(sK), 16, 1024);
+      const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), PANEL, 1024);
+      const uint32_t s_tm = tmem + t * 128, o_tm = tmem + 256 + t * 128;
+      // Each GEMM is one straight-line run of MMAs (compile-time trip counts).
+      auto issue_qk = [&](int j) {
+        const uint32_t koff = (j % kStages) * TILE;
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
-          kf::umma_ss(tmem + t * 128, kf::make_sdesc(qb + off, 16, 1024),
-                      kf::make_sdesc(kb + off, 16, 1024), idesc_qk, kk > 0);
+          kf::umma_ss(s_tm, kf::sdesc_at(dq, off), kf::sdesc_at(dk, koff + off), idesc_qk, kk > 0);
         }
       };
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t vb = sv_u + (j % kStages) * TILE;
+      auto issue_pv = [&](int j) {
+        const uint32_t voff = (j % kStages) * TILE;
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          kf::umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                      kf::make_sdesc(vb + kk * 2048, PANEL, 1024), idesc_pv, (j > 0 || kk > 0));
-        }
+        for (int kk = 0; kk < kBlockN / 16; ++kk)
+          kf::umma_ts(o_tm, s_tm + kk * 8, kf::sdesc_at(dv, voff + kk * 2048), idesc_pv,
+                      (j > 0 || kk > 0));
       };
       bool ok = wait_bar(&bars->q_full, 0, bars, p.status) &&
                 wait_bar(&bars->k_full[0], 0, bars, p.status);
       if (ok) {
         kf::tc_fence_after();
-        for (int t = 0; t < nt; ++t) {
-          issue_qk(t, 0);
-          kf::umma_commit(&bars->s_full[t]);
-        }
+        issue_qk(0);
+        kf::umma_commit(&bars->s_full[t]);
         kf::umma_commit(&bars->k_empty[0]);
       }
       for (int j = 0; ok && j < nblk; ++j) {
@@ -228,20 +241,17 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         const uint32_t ph1 = ((j + 1) / kStages) & 1;
         if (!(ok = wait_bar(&bars->v_full[s], ph, bars, p.status))) break;
         if (more && !(ok = wait_bar(&bars->k_full[s1], ph1, bars, p.status))) break;
-        for (int t = 0; t < nt; ++t) {
-          if (!(ok = wait_bar(&bars->p_full[t], j & 1, bars, p.status))) break;
-          kf::tc_fence_after();
-          issue_pv(t, j);
-          if (more) {
-            issue_qk(t, j + 1);
-            kf::umma_commit(&bars->s_full[t]);
-          }
-        }
-        if (!ok) break;
+        if (!(ok = wait_bar(&bars->p_full[t], j & 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        issue_pv(j);
         kf::umma_commit(&bars->v_empty[s]);
-        if (more) kf::umma_commit(&bars->k_empty[s1]);
+        if (more) {
+          issue_qk(j + 1);
+          kf::umma_commit(&bars->s_full[t]);
+          kf::umma_commit(&bars->k_empty[s1]);
+        }
       }
-      kf::umma_commit(&bars->o_final);
+      kf::umma_commit(&bars->o_final[t]);
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -261,23 +271,27 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
       kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
       kf::tmem_wait_ld();
-      float x[128];
       const int key0 = j * kBlockN;
       const bool need_mask = (key0 + kBlockN > p.Sk) || (p.causal && key0 + kBlockN - 1 > ti.row0[t]);
-      float mx = -INFINITY;
       if (need_mask) {
         const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : kBlockN);
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          x[c] = c < lim ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, x[c]);
-        }
-      } else {
+        for (int c = 0; c < 128; ++c)
+          if (c >= lim) sr[c] = 0xFF800000u;  // -inf
+      }
+      // Row max of the raw scores (the scale is positive, so it commutes),
+      // four independent chains of three-input maxima.
+      float mx;
+      {
+        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          x[c] = __uint_as_float(sr[c]) * p.scale_log2;
-          mx = fmaxf(mx, x[c]);
+        for (int c = 0; c < 128; c += 8) {
+          a0 = kf::fmax3(a0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
+          a1 = kf::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          a2 = kf::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          a3 = kf::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
         }
+        mx = kf::fmax3(a0, a1, fmaxf(a2, a3)) * p.scale_log2;
       }
       float alpha = 1.f;
       bool rescale_o = false;
@@ -290,15 +304,45 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       }
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
       l_sum *= alpha;
-      uint32_t pk[64];
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = kf::ex2(x[2 * c] - m_use), p1 = kf::ex2(x[2 * c + 1] - m_use);
-        sum += p0 + p1;
-        pk[c] = kf::pack2<BF16>(p0, p1);
+      // Tile 0 exponentiates block j after tile 1 finished block j-1, tile 1
+      // after tile 0 finished block j: the two warps sharing each SM
+      // sub-partition never compete for MUFU and issue slots.
+      if (nt == 2 && (t == 1 || j > 0)) {
+        if (!(ok = wait_bar(&bars->turn[t], (t == 1 ? j : j - 1) & 1, bars, p.status))) break;
       }
-      l_sum += sum;
+      // P = 2^(s * scale_log2 - m): the argument is one packed fma per pair;
+      // masked blocks (-inf entries) use MUFU only, full blocks send
+      // kPolyPairs of every 8 pairs to the fp32-pipe polynomial.
+      const uint64_t scl = kf::f2(p.scale_log2, p.scale_log2), negm = kf::f2(-m_use, -m_use);
+      uint32_t pk[64];
+      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          float x0, x1;
+          kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+          const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
+          acc[c & 3] = kf::add2(acc[c & 3], kf::f2(p0, p1));
+          pk[c] = kf::pack2<BF16>(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          float x0, x1;
+          kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+          const uint64_t pp = (c & 7) < kPolyPairs ? kf::exp2_poly2(x0, x1) : kf::f2(kf::ex2(x0), kf::ex2(x1));
+          acc[c & 3] = kf::add2(acc[c & 3], pp);
+          float p0, p1;
+          kf::f2_split(pp, p0, p1);
+          pk[c] = kf::pack2<BF16>(p0, p1);
+        }
+      }
+      {
+        float s0, s1;
+        kf::f2_split(kf::add2(kf::add2(acc[0], acc[1]), kf::add2(acc[2], acc[3])), s0, s1);
+        l_sum += s0 + s1;
+      }
+      if (nt == 2) kf::mbar_arrive(&bars->turn[t ^ 1]);
       kf::tmem_st32(lane_base + s_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
       kf::tmem_st32(lane_base + s_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
       if (__any_sync(0xffffffffu, rescale_o)) {
@@ -317,7 +361,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::mbar_arrive(&bars->p_full[t]);
     }
     // ---------------------------------------------------------- epilogue
-    if (ok && wait_bar(&bars->o_final, 0, bars, p.status)) {
+    if (ok && wait_bar(&bars->o_final[t], 0, bars, p.status)) {
       kf::tc_fence_after();
       const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
       const bool row_ok = row < p.Sq;

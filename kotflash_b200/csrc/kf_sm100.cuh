@@ -36,6 +36,68 @@ KF_DEVI float ex2(float x) {
   return y;
 }
 
+// ---------------------------------------------------------------- packed fp32
+// sm_100 executes fp32 add/sub/fma on register pairs (one instruction for two
+// lanes of work); a pair travels as one 64-bit register.
+KF_DEVI uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+KF_DEVI void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+KF_DEVI uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+KF_DEVI uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+KF_DEVI uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// max of three fp32 values (sm_100 three-input form)
+KF_DEVI float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of arguments on the fp32 pipe instead of the MUFU unit,
+// for kernels whose exponentials outrun MUFU throughput.  Method: split
+// x = j + f with j = rint(x) by the magic-number addition (x + 1.5 * 2^23
+// leaves rint(x) in the low mantissa bits), evaluate 2^f on [-0.5, 0.5] with
+// a degree-3 polynomial whose coefficients are a relative-error minimax fit
+// (Remez exchange, max relative error 1.3e-4 in fp32 arithmetic), then add j
+// to the exponent field.  Arguments are clamped to >= -125 so the exponent
+// cannot underflow; results for x < -125 are ~2^-125 instead of 0, which is
+// immaterial next to softmax sums >= 1.  Intended for finite x <= 127.
+KF_DEVI uint64_t exp2_poly2(float x0, float x1) {
+  const uint64_t magic = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
+  const uint64_t c0 = 0x3F7FFB493F7FFB49ull;     // 0.99992806
+  const uint64_t c1 = 0x3F31798D3F31798Dull;     // 0.69326097
+  const uint64_t c2 = 0x3E786F0D3E786F0Dull;     // 0.24261113
+  const uint64_t c3 = 0x3D61FBB03D61FBB0ull;     // 0.05517167
+  const uint64_t x = f2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = add2(x, magic);
+  const uint64_t f = sub2(x, sub2(t, magic));
+  uint64_t p = fma2(c3, f, c2);
+  p = fma2(p, f, c1);
+  p = fma2(p, f, c0);
+  uint32_t p0, p1, t0, t1;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(p0), "=r"(p1) : "l"(p));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(p0 + (t0 << 23)), "r"(p1 + (t1 << 23)));
+  return r;
+}
+
 // Wait budget for every device-side spin: about one second of wall time.
 constexpr uint64_t kWaitBudgetNs = 1000000000ull;
 
@@ -252,6 +314,24 @@ KF_DEVI uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_byt
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)kSwizzle128B << 61;
+  return d;
+}
+
+// The same descriptor kept as two 32-bit words so that an issue loop can move
+// the start address with one 32-bit add: the low word holds start >> 4 in
+// bits [0,14) and LBO, the high word SBO, version and swizzle.  Shared memory
+// addresses stay below 256 KB, so start >> 4 never carries out of its field.
+struct SDesc {
+  uint32_t lo, hi;
+};
+KF_DEVI SDesc make_sdesc_split(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  const uint64_t d = make_sdesc(saddr, lbo_bytes, sbo_bytes);
+  return SDesc{(uint32_t)d, (uint32_t)(d >> 32)};
+}
+// Descriptor of `base` moved by `bytes` (a multiple of 16).
+KF_DEVI uint64_t sdesc_at(SDesc base, uint32_t bytes) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(base.lo + (bytes >> 4)), "r"(base.hi));
   return d;
 }
 
