@@ -23,19 +23,29 @@
 //                 dV  += P^T dO     (TS MMA, A = P^T in TMEM)
 //                 dK  += dS^T Q     (TS MMA, A = dS^T in TMEM)
 //                 dQ^T = K^T dS^T   (SS MMA, both operands MN-major)
-//               Issue order dV(s), S^T(s+1), dK(s), dQ^T(s), dP^T(s+1) hides
-//               each softmax phase behind two or three GEMMs.
-//               dQ^T (thread = head-dim lane, double-buffered in TMEM) is
+//               Two threads issue the MMAs: one the score GEMMs (S^T, dP^T),
+//               one the gradient GEMMs (dV, dK, dQ^T).  On sm_100 the tensor
+//               pipe keeps almost no MMAs queued, so the barrier waits, fences
+//               and commits of a single issuing thread would idle it; with two
+//               issuers each one's synchronisation is covered by the other's
+//               MMAs.  S^T/P^T and dP^T/dS^T are double-buffered in TMEM and
+//               dS^T in shared memory; dQ^T(s) is written over the dP^T/dS^T
+//               buffer of its own step once dK(s) has read it (MMAs of one
+//               thread execute in order), which is what frees the TMEM for
+//               the second S^T buffer.  Every loop-carried dependency thus
+//               spans two steps.
+//               dQ^T (thread = head-dim lane) is
 //               staged in 128-byte swizzled shared memory by a dedicated
 //               warpgroup and added into the fp32 workspace with TMA
 //               reduce-add (cp.reduce.async.bulk.tensor), off the LSU path.  dK/dV accumulate in TMEM for the whole group and are
 //               written once, so no dK/dV partial buffers exist.
 //   3. finish : dQ = scale * workspace, cast to the input dtype.
-// Tensor memory (512 columns): dV [0,128) dK [128,256) S^T [256,320)
-// dP^T [320,384) dQ^T buffers [384,448) [448,512).
+// Tensor memory (512 columns): dV [0,128) dK [128,256), S^T/P^T buffers
+// [256,320) [320,384), dP^T/dS^T/dQ^T buffers [384,448) [448,512).
 // Warps: 0-7 softmax (two warpgroups split the 64 query columns), 8-11 dQ
-// drain, 12 TMA producer, 13 TMEM allocator + MMA issuer; 0-7 also write the
-// dV (warps 0-3) and dK (warps 4-7) epilogue.
+// drain, 12 TMA producer, 13 TMEM allocator + score-GEMM issuer, 14
+// gradient-GEMM issuer; 0-7 also write the dV (warps 0-3) and dK (warps 4-7)
+// epilogue.
 #include <math.h>
 
 #include "kf_host.h"
@@ -45,8 +55,15 @@ namespace {
 
 constexpr int kBM = 64;    // query rows per step
 constexpr int kBN = 128;   // keys per CTA
-constexpr int kStages = 2;
-constexpr int kThreads = 448;  // 14 warps
+constexpr int kStages = 3;  // Q/dO/statistics ring
+constexpr int kThreads = 480;  // 15 warps
+// TMEM columns
+constexpr uint32_t kColDV = 0, kColDK = 128, kColS = 256, kColDP = 384;
+// 16-bit P^T / dS^T of query columns [32 wg, 32 wg + 32) are packed into the
+// first 16 of the 32 fp32 columns that held that warpgroup's S^T / dP^T, so a
+// warpgroup never overwrites columns the other one still has to read.  MMA
+// k-step kk (16 queries) therefore reads packed column 32 (kk / 2) + 8 (kk % 2).
+__host__ __device__ constexpr uint32_t packed_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
@@ -65,8 +82,9 @@ struct BwdParams {
 struct __align__(8) BwdBarriers {
   uint64_t kv_full;
   uint64_t qdo_full[kStages], qdo_empty[kStages];
-  uint64_t s_ready, dp_ready, p_ready, ds_ready;
-  uint64_t dq_full[2], dq_empty[2];
+  uint64_t s_ready[2], p_ready[2], p_free[2];     // per S^T/P^T buffer
+  uint64_t dp_ready[2], ds_ready[2], dq_full[2];  // per dP^T/dS^T/dQ^T buffer
+  uint64_t ds_free[2];                            // dQ^T drained: buffer reusable
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -78,8 +96,8 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, BwdBarr
   const uint64_t t0 = kf::global_timer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (kf::mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
+    if (kf::mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    if ((++spins & 15u) == 0) {
       if (*(volatile int*)&bars->abort_flag) return false;
       if (kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
         *(volatile int*)&bars->abort_flag = 1;
@@ -112,9 +130,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   uint8_t* sV = sK + 2 * KPANEL;                    // 2 panels
   uint8_t* sQ = sV + 2 * KPANEL;                    // [stage][2 panels]
   uint8_t* sdO = sQ + kStages * 2 * QPANEL;         // [stage][2 panels]
-  uint8_t* sdS = sdO + kStages * 2 * QPANEL;        // 128 rows x 128 B
-  uint8_t* sDQ = sdS + KPANEL;                      // [2 buffers][2 halves][D rows][32 fp32]
-  float* sLD = reinterpret_cast<float*>(sDQ + 2 * 2 * 128 * 128);  // [stage][lse2 64 | delta 64]
+  uint8_t* sdS = sdO + kStages * 2 * QPANEL;        // [2 buffers][128 rows x 128 B]
+  uint8_t* sDQ = sdS + 2 * KPANEL;                  // [2 halves][D rows][32 fp32]
+  float* sLD = reinterpret_cast<float*>(sDQ + 2 * 128 * 128);  // [stage][lse2 64 | delta 64]
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(sLD + kStages * 2 * kBM);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -134,13 +152,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::mbar_init(&bars->qdo_full[s], 1);
       kf::mbar_init(&bars->qdo_empty[s], 1);
     }
-    kf::mbar_init(&bars->s_ready, 1);
-    kf::mbar_init(&bars->dp_ready, 1);
-    kf::mbar_init(&bars->p_ready, 256);
-    kf::mbar_init(&bars->ds_ready, 256);
     for (int s = 0; s < 2; ++s) {
+      kf::mbar_init(&bars->s_ready[s], 1);
+      kf::mbar_init(&bars->p_ready[s], 256);
+      kf::mbar_init(&bars->p_free[s], 1);
+      kf::mbar_init(&bars->dp_ready[s], 1);
+      kf::mbar_init(&bars->ds_ready[s], 256);
       kf::mbar_init(&bars->dq_full[s], 1);
-      kf::mbar_init(&bars->dq_empty[s], 128);
+      kf::mbar_init(&bars->ds_free[s], 128);
     }
     kf::mbar_init(&bars->mma_done, 1);
     bars->abort_flag = 0;
@@ -183,87 +202,80 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         bulk_load(sLD + st * 2 * kBM + kBM, p.delta + row_off, kBM * 4, &bars->qdo_full[st]);
       }
     }
-  } else if (warp == 13) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 13 || warp == 14) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0 && nsteps > 0) {
       const uint32_t idesc_s = kf::make_idesc_f16(BF16, 128, kBM, 0, 0);
       const uint32_t idesc_kv = kf::make_idesc_f16(BF16, 128, d_pad16, 0, 1);
       const uint32_t idesc_q = kf::make_idesc_f16(BF16, 128, kBM, 1, 1);
-      const uint32_t sk_u = kf::smem_u32(sK), sv_u = kf::smem_u32(sV);
-      const uint32_t sq_u = kf::smem_u32(sQ), sdo_u = kf::smem_u32(sdO), sds_u = kf::smem_u32(sdS);
-      // Each GEMM is one straight-line run of MMAs (compile-time trip counts):
-      // branches between consecutive tcgen05.mma slow their issue down.
-      auto issue_s = [&](int s) {  // S^T = K Q^T
-        const uint32_t qb = sq_u + (s % kStages) * 2 * QPANEL;
-#pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-          const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
-          const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
-          kf::umma_ss(tmem + 256, kf::make_sdesc(sk_u + ka, 16, 1024),
-                      kf::make_sdesc(qb + qa, 16, 1024), idesc_s, kk > 0);
-        }
-      };
-      auto issue_dp = [&](int s) {  // dP^T = V dO^T
-        const uint32_t dob = sdo_u + (s % kStages) * 2 * QPANEL;
-#pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-          const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
-          const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
-          kf::umma_ss(tmem + 320, kf::make_sdesc(sv_u + ka, 16, 1024),
-                      kf::make_sdesc(dob + qa, 16, 1024), idesc_s, kk > 0);
-        }
-      };
-      // Issue order per step s:  dV(s)  S^T(s+1)  dK(s)  dQ^T(s)  dP^T(s+1)
-      // so the softmax's P phase of step s+1 overlaps dK/dQ^T/dP^T and its dS
-      // phase of step s overlaps dV(s)/S^T(s+1).
-      bool ok = wait_bar(&bars->kv_full, 0, bars, p.status) &&
-                wait_bar(&bars->qdo_full[0], 0, bars, p.status);
-      if (ok) {
-        kf::tc_fence_after();
-        issue_s(0);
-        kf::umma_commit(&bars->s_ready);
-        issue_dp(0);
-        kf::umma_commit(&bars->dp_ready);
-      }
-      for (int s = 0; ok && s < nsteps; ++s) {
-        const int st = s % kStages;
-        const uint32_t qb = sq_u + st * 2 * QPANEL, dob = sdo_u + st * 2 * QPANEL;
-        const bool more = s + 1 < nsteps;
-        if (!(ok = wait_bar(&bars->p_ready, s & 1, bars, p.status))) break;
-        kf::tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          kf::umma_ts(tmem + 0, tmem + 256 + kk * 8, kf::make_sdesc(dob + kk * 2048, QPANEL, 1024),
-                      idesc_kv, (s > 0 || kk > 0));
-        if (more) {
-          if (!(ok = wait_bar(&bars->qdo_full[(s + 1) % kStages], ((s + 1) / kStages) & 1, bars,
-                              p.status)))
-            break;
+      // Descriptors are built once; each MMA adds a compile-time offset.
+      const kf::SDesc dk_k = kf::make_sdesc_split(kf::smem_u32(sK), 16, 1024);
+      const kf::SDesc dk_v = kf::make_sdesc_split(kf::smem_u32(sV), 16, 1024);
+      const kf::SDesc dk_q = kf::make_sdesc_split(kf::smem_u32(sQ), 16, 1024);
+      const kf::SDesc dk_do = kf::make_sdesc_split(kf::smem_u32(sdO), 16, 1024);
+      const kf::SDesc dm_q = kf::make_sdesc_split(kf::smem_u32(sQ), QPANEL, 1024);
+      const kf::SDesc dm_do = kf::make_sdesc_split(kf::smem_u32(sdO), QPANEL, 1024);
+      const kf::SDesc dm_k = kf::make_sdesc_split(kf::smem_u32(sK), KPANEL, 1024);
+      const kf::SDesc dm_ds = kf::make_sdesc_split(kf::smem_u32(sdS), KPANEL, 1024);
+      bool ok = wait_bar(&bars->kv_full, 0, bars, p.status);
+      if (warp == 13) {
+        // score GEMMs: S^T(s) = K Q^T, dP^T(s) = V dO^T into buffer s & 1
+        for (int s = 0; ok && s < nsteps; ++s) {
+          const int st = s % kStages, buf = s & 1;
+          const uint32_t qoff = st * 2 * QPANEL;
+          if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
+          // P^T(s-2), which overlays S^T in this buffer, has been read by dV(s-2)
+          if (s >= 2 && !(ok = wait_bar(&bars->p_free[buf], ((s - 2) >> 1) & 1, bars, p.status))) break;
           kf::tc_fence_after();
-          issue_s(s + 1);
-          kf::umma_commit(&bars->s_ready);
-        }
-        if (!(ok = wait_bar(&bars->ds_ready, s & 1, bars, p.status))) break;
-        kf::tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          kf::umma_ts(tmem + 128, tmem + 320 + kk * 8, kf::make_sdesc(qb + kk * 2048, QPANEL, 1024),
-                      idesc_kv, (s > 0 || kk > 0));
-        kf::umma_commit(&bars->qdo_empty[st]);
-        const int buf = s & 1;
-        if (!(ok = wait_bar(&bars->dq_empty[buf], ((s >> 1) & 1) ^ 1, bars, p.status))) break;
-        kf::tc_fence_after();
+          for (int kk = 0; kk < KS; ++kk) {
+            const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
+            const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
+            kf::umma_ss(tmem + kColS + buf * 64, kf::sdesc_at(dk_k, ka), kf::sdesc_at(dk_q, qoff + qa),
+                        idesc_s, kk > 0);
+          }
+          kf::umma_commit(&bars->s_ready[buf]);
+          // dQ^T(s-2) has been drained from buffer `buf` (so dK(s-2) and
+          // dQ^T(s-2) are also done with dS^T(s-2) in TMEM and shared memory)
+          if (s >= 2 && !(ok = wait_bar(&bars->ds_free[buf], ((s - 2) >> 1) & 1, bars, p.status))) break;
+          kf::tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          kf::umma_ss(tmem + 384 + buf * 64, kf::make_sdesc(sk_u + kk * 2048, KPANEL, 1024),
-                      kf::make_sdesc(sds_u + kk * 2048, KPANEL, 1024), idesc_q, kk > 0);
-        kf::umma_commit(&bars->dq_full[buf]);
-        if (more) {
-          issue_dp(s + 1);
-          kf::umma_commit(&bars->dp_ready);
+          for (int kk = 0; kk < KS; ++kk) {
+            const uint32_t ka = (kk >> 2) * KPANEL + (kk & 3) * 32;
+            const uint32_t qa = (kk >> 2) * QPANEL + (kk & 3) * 32;
+            kf::umma_ss(tmem + kColDP + buf * 64, kf::sdesc_at(dk_v, ka), kf::sdesc_at(dk_do, qoff + qa),
+                        idesc_s, kk > 0);
+          }
+          kf::umma_commit(&bars->dp_ready[buf]);
         }
+      } else {
+        // gradient GEMMs: dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T
+        for (int s = 0; ok && s < nsteps; ++s) {
+          const int st = s % kStages, buf = s & 1;
+          const uint32_t qoff = st * 2 * QPANEL;
+          if (!(ok = wait_bar(&bars->p_ready[buf], (s >> 1) & 1, bars, p.status))) break;
+          kf::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            kf::umma_ts(tmem + kColDV, tmem + kColS + buf * 64 + packed_col(kk),
+                        kf::sdesc_at(dm_do, qoff + kk * 2048), idesc_kv, (s > 0 || kk > 0));
+          kf::umma_commit(&bars->p_free[buf]);
+          if (!(ok = wait_bar(&bars->ds_ready[buf], (s >> 1) & 1, bars, p.status))) break;
+          kf::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            kf::umma_ts(tmem + kColDK, tmem + kColDP + buf * 64 + packed_col(kk),
+                        kf::sdesc_at(dm_q, qoff + kk * 2048), idesc_kv, (s > 0 || kk > 0));
+          kf::umma_commit(&bars->qdo_empty[st]);
+          // dQ^T(s) overwrites this step's dS^T in TMEM after dK(s) read it
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            kf::umma_ss(tmem + kColDP + buf * 64, kf::sdesc_at(dm_k, kk * 2048),
+                        kf::sdesc_at(dm_ds, buf * KPANEL + kk * 2048), idesc_q, kk > 0);
+          kf::umma_commit(&bars->dq_full[buf]);
+        }
+        kf::umma_commit(&bars->mma_done);
       }
-      kf::umma_commit(&bars->mma_done);
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ P / dS (thread = key)
@@ -274,49 +286,70 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int key = n * kBN + kr;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
-    for (int s = 0; ok && s < nsteps; ++s) {
-      const int st = s % kStages;
+    int i_step = i0;  // query block of step s (steps walk heads, then blocks i0..nqb-1)
+    for (int s = 0; ok && s < nsteps; ++s, i_step = (i_step + 1 == p.nqb) ? i0 : i_step + 1) {
+      const int st = s % kStages, buf = s & 1;
       if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
-      if (!(ok = wait_bar(&bars->s_ready, s & 1, bars, p.status))) break;
+      // The row statistics are read into registers before waiting for S^T:
+      // during the step the tensor cores keep shared memory busy, and a load
+      // issued after S^T is ready would sit on the critical path.
+      const float4* lse4 = reinterpret_cast<const float4*>(sLD + st * 2 * kBM + c0);
+      const float4* dlt4 = reinterpret_cast<const float4*>(sLD + st * 2 * kBM + kBM + c0);
+      float4 lv[8];
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) lv[c4] = lse4[c4];
+      const int q0 = i_step * kBM + c0;
+      const uint32_t col_s = kColS + buf * 64;
+      if (!(ok = wait_bar(&bars->s_ready[buf], (s >> 1) & 1, bars, p.status))) break;
       kf::tc_fence_after();
-      int h, i;
-      step_coords(s, h, i);
       uint32_t sr[32];
-      kf::tmem_ld32(lane_base + 256 + c0, sr);
+      kf::tmem_ld32(lane_base + col_s + c0, sr);
       kf::tmem_wait_ld();
-      const float* lse2 = sLD + st * 2 * kBM + c0;
-      const float* dlt = sLD + st * 2 * kBM + kBM + c0;
-      const int q0 = i * kBM + c0;
       // visible iff key < Sk and (not causal or key <= q): columns c >= first_q
       const int first_q = p.causal ? key - q0 : 0;
       const bool key_ok = key < p.Sk;
       float pr[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 l = lv[c4];
+        pr[4 * c4 + 0] = kf::ex2(__uint_as_float(sr[4 * c4 + 0]) * p.scale_log2 - l.x);
+        pr[4 * c4 + 1] = kf::ex2(__uint_as_float(sr[4 * c4 + 1]) * p.scale_log2 - l.y);
+        pr[4 * c4 + 2] = kf::ex2(__uint_as_float(sr[4 * c4 + 2]) * p.scale_log2 - l.z);
+        pr[4 * c4 + 3] = kf::ex2(__uint_as_float(sr[4 * c4 + 3]) * p.scale_log2 - l.w);
+      }
+      if (!key_ok || first_q > 0) {  // only blocks on the causal diagonal or past Sk
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (!key_ok || c < first_q) pr[c] = 0.f;
+      }
       uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float x = __uint_as_float(sr[c]) * p.scale_log2 - lse2[c];
-        pr[c] = (key_ok && c >= first_q) ? kf::ex2(x) : 0.f;
-      }
-#pragma unroll
       for (int c = 0; c < 16; ++c) pk[c] = kf::pack2<BF16>(pr[2 * c], pr[2 * c + 1]);
-      kf::tmem_st16(lane_base + 256 + wg * 16, pk);
+      kf::tmem_st16(lane_base + col_s + c0, pk);  // over this warpgroup's own S^T columns
       kf::tmem_wait_st();
       kf::tc_fence_before();
-      kf::mbar_arrive(&bars->p_ready);
+      kf::mbar_arrive(&bars->p_ready[buf]);
 
-      if (!(ok = wait_bar(&bars->dp_ready, s & 1, bars, p.status))) break;
+      const uint32_t col_dp = kColDP + buf * 64;
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) lv[c4] = dlt4[c4];
+      if (!(ok = wait_bar(&bars->dp_ready[buf], (s >> 1) & 1, bars, p.status))) break;
       kf::tc_fence_after();
       uint32_t dr[32];
-      kf::tmem_ld32(lane_base + 320 + c0, dr);
+      kf::tmem_ld32(lane_base + col_dp + c0, dr);
       kf::tmem_wait_ld();
       uint32_t dk[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c)
-        dk[c] = kf::pack2<BF16>(pr[2 * c] * (__uint_as_float(dr[2 * c]) - dlt[2 * c]),
-                                pr[2 * c + 1] * (__uint_as_float(dr[2 * c + 1]) - dlt[2 * c + 1]));
-      kf::tmem_st16(lane_base + 320 + wg * 16, dk);
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 dl = lv[c4];
+        dk[2 * c4] = kf::pack2<BF16>(pr[4 * c4 + 0] * (__uint_as_float(dr[4 * c4 + 0]) - dl.x),
+                                     pr[4 * c4 + 1] * (__uint_as_float(dr[4 * c4 + 1]) - dl.y));
+        dk[2 * c4 + 1] = kf::pack2<BF16>(pr[4 * c4 + 2] * (__uint_as_float(dr[4 * c4 + 2]) - dl.z),
+                                         pr[4 * c4 + 3] * (__uint_as_float(dr[4 * c4 + 3]) - dl.w));
+      }
+      kf::tmem_st16(lane_base + col_dp + c0, dk);  // over this warpgroup's own dP^T columns
       // dS^T row -> shared memory, 128-byte swizzle (16-byte chunk c at c ^ (row & 7))
-      uint8_t* row_ptr = sdS + kr * 128;
+      uint8_t* row_ptr = sdS + buf * KPANEL + kr * 128;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(row_ptr + (((wg * 4 + j) ^ (kr & 7)) << 4)) =
@@ -324,7 +357,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       kf::fence_proxy_async_smem();
       kf::tmem_wait_st();
       kf::tc_fence_before();
-      kf::mbar_arrive(&bars->ds_ready);
+      kf::mbar_arrive(&bars->ds_ready[buf]);
     }
   } else if (warp < 12) {
     // ------------------------------------------------------------ dQ drain (thread = head-dim lane)
@@ -334,39 +367,44 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int d_rows = p.D;                 // multiple of 8, so halves stay 1024-aligned
     bool ok = true;
     for (int s = 0; ok && s < nsteps; ++s) {
-      const int buf = s & 1;
+      const int buf = s & 1;  // TMEM buffer and shared-memory staging buffer
       if (!(ok = wait_bar(&bars->dq_full[buf], (s >> 1) & 1, bars, p.status))) break;
       kf::tc_fence_after();
       uint32_t v[64];
-      kf::tmem_ld32(lane_base + 384 + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      kf::tmem_ld32(lane_base + 416 + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      kf::tmem_ld32(lane_base + kColDP + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      kf::tmem_ld32(lane_base + kColDP + buf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       kf::tmem_wait_ld();
       kf::tc_fence_before();
-      kf::mbar_arrive(&bars->dq_empty[buf]);
-      // staging buffer `buf` was last used two steps ago: let that reduce finish reading
-      if (dl == 0) kf::bulk_wait_group_read<1>();
-      kf::named_bar_sync(1, 128);
-      uint8_t* stage = sDQ + buf * 2 * 128 * 128;
-      if (dl < d_rows) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint8_t* row_ptr = stage + h * d_rows * 128 + dl * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(row_ptr + ((c ^ (dl & 7)) << 4)) =
-                make_uint4(v[h * 32 + 4 * c], v[h * 32 + 4 * c + 1], v[h * 32 + 4 * c + 2],
-                           v[h * 32 + 4 * c + 3]);
-        }
-      }
-      kf::fence_proxy_async_smem();
-      kf::named_bar_sync(1, 128);
+      kf::mbar_arrive(&bars->ds_free[buf]);
+      // The staging tile has two halves (query columns 0-31 and 32-63), each
+      // reduced by its own bulk group, so the reduce of one half overlaps
+      // the staging of the other.
+      int row0 = 0;
       if (dl == 0) {
         int h, i;
         step_coords(s, h, i);
-        const int row0 = (int)((((int64_t)b * p.Hq + h) * p.nqb + i) * p.D);
-        kf::tma_reduce_add_2d(&map_dq, stage, 0, row0);
-        kf::tma_reduce_add_2d(&map_dq, stage + d_rows * 128, 32, row0);
-        kf::bulk_commit_group();
+        row0 = (int)((((int64_t)b * p.Hq + h) * p.nqb + i) * p.D);
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint8_t* half = sDQ + hf * d_rows * 128;
+        // this half was last reduced two bulk groups ago
+        if (dl == 0) kf::bulk_wait_group_read<1>();
+        kf::named_bar_sync(1, 128);
+        if (dl < d_rows) {
+          uint8_t* row_ptr = half + dl * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(row_ptr + ((c ^ (dl & 7)) << 4)) =
+                make_uint4(v[hf * 32 + 4 * c], v[hf * 32 + 4 * c + 1], v[hf * 32 + 4 * c + 2],
+                           v[hf * 32 + 4 * c + 3]);
+        }
+        kf::fence_proxy_async_smem();
+        kf::named_bar_sync(1, 128);
+        if (dl == 0) {
+          kf::tma_reduce_add_2d(&map_dq, half, hf * 32, row0);
+          kf::bulk_commit_group();
+        }
       }
     }
     if (dl == 0) kf::bulk_wait_group<0>();
@@ -387,7 +425,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       for (int c0 = 0; c0 < d_pad16; c0 += 32) {
         uint32_t ov[32];
         if (have) {
-          kf::tmem_ld32(lane_base + (is_dk ? 128 : 0) + c0, ov);
+          kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0, ov);
           kf::tmem_wait_ld();
         } else {
 #pragma unroll
@@ -501,8 +539,8 @@ template <bool BF16, int KS>
 int launch_bwd_main(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                     const CUtensorMap& mdo, const CUtensorMap& mdq, const BwdParams& p,
                     cudaStream_t st) {
-  const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 128 * 128 +
-                      2 * 2 * 128 * 128 + kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
+  const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 2 * 128 * 128 +
+                      2 * 128 * 128 + kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
   auto kern = bwd_kernel<BF16, KS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: cannot reserve %zu bytes of shared memory", smem);

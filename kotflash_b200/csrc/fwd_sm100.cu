@@ -79,8 +79,8 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, FwdBarr
   const uint64_t t0 = kf::global_timer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (kf::mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
+    if (kf::mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    if ((++spins & 15u) == 0) {
       if (*(volatile int*)&bars->abort_flag) return false;
       if (kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
         *(volatile int*)&bars->abort_flag = 1;

@@ -136,6 +136,22 @@ KF_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Same test, but a thread whose phase is still open is suspended until the
+// phase completes or `hint_ns` nanoseconds pass, instead of returning at
+// once: waiting warps then stop competing for issue slots with the warps
+// that do the work.
+KF_DEVI bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on the phase with the given parity.  Returns false (and sets
 // *status to 1, the timeout code) once `budget_ns` of wall time is spent, so
 // no wait can run forever.
