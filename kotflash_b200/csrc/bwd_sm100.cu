@@ -48,6 +48,8 @@
 // epilogue.
 #include <math.h>
 
+#include <algorithm>
+
 #include "kf_host.h"
 #include "kf_sm100.cuh"
 
@@ -65,6 +67,10 @@ constexpr uint32_t kColDV = 0, kColDK = 128, kColS = 256, kColDP = 384;
 // k-step kk (16 queries) therefore reads packed column 32 (kk / 2) + 8 (kk % 2).
 __host__ __device__ constexpr uint32_t packed_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
 constexpr float kLog2e = 1.4426950408889634f;
+#ifndef KF_BWD_POLY_QUADS
+#define KF_BWD_POLY_QUADS 0
+#endif
+constexpr int kPolyQuads = KF_BWD_POLY_QUADS;
 
 struct BwdParams {
   uint16_t* dk;
@@ -309,13 +315,25 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const int first_q = p.causal ? key - q0 : 0;
       const bool key_ok = key < p.Sk;
       float pr[32];
+      // kPolyQuads of the 8 groups of four exponentials run as the fp32-pipe
+      // polynomial, the rest on MUFU (x <= 0 here; padded rows give x = -inf,
+      // which the polynomial clamps to a ~2^-125 P that meets zero dO / dP).
 #pragma unroll
       for (int c4 = 0; c4 < 8; ++c4) {
         const float4 l = lv[c4];
-        pr[4 * c4 + 0] = kf::ex2(__uint_as_float(sr[4 * c4 + 0]) * p.scale_log2 - l.x);
-        pr[4 * c4 + 1] = kf::ex2(__uint_as_float(sr[4 * c4 + 1]) * p.scale_log2 - l.y);
-        pr[4 * c4 + 2] = kf::ex2(__uint_as_float(sr[4 * c4 + 2]) * p.scale_log2 - l.z);
-        pr[4 * c4 + 3] = kf::ex2(__uint_as_float(sr[4 * c4 + 3]) * p.scale_log2 - l.w);
+        const float x0 = __uint_as_float(sr[4 * c4 + 0]) * p.scale_log2 - l.x;
+        const float x1 = __uint_as_float(sr[4 * c4 + 1]) * p.scale_log2 - l.y;
+        const float x2 = __uint_as_float(sr[4 * c4 + 2]) * p.scale_log2 - l.z;
+        const float x3 = __uint_as_float(sr[4 * c4 + 3]) * p.scale_log2 - l.w;
+        if (c4 < kPolyQuads) {
+          kf::f2_split(kf::exp2_poly2(x0, x1), pr[4 * c4 + 0], pr[4 * c4 + 1]);
+          kf::f2_split(kf::exp2_poly2(x2, x3), pr[4 * c4 + 2], pr[4 * c4 + 3]);
+        } else {
+          pr[4 * c4 + 0] = kf::ex2(x0);
+          pr[4 * c4 + 1] = kf::ex2(x1);
+          pr[4 * c4 + 2] = kf::ex2(x2);
+          pr[4 * c4 + 3] = kf::ex2(x3);
+        }
       }
       if (!key_ok || first_q > 0) {  // only blocks on the causal diagonal or past Sk
 #pragma unroll
@@ -454,13 +472,18 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   }
 }
 
-// Delta = rowsum(O * dO) and LSE * log2(e), one warp per (padded) row.
+// Delta = rowsum(O * dO) and LSE * log2(e) per (padded) query row, plus the
+// zero fill of the fp32 dQ accumulator.  Sixteen threads share a row (16-byte
+// loads of O and dO, eight elements each); the grid strides over rows so
+// every SM keeps many loads in flight.
 struct PrepArgs {
   const uint16_t* o;
   const uint16_t* dout;
   const float* lse;
   float* lse2;
   float* delta;
+  float4* acc;         // dQ accumulator, zeroed here
+  int64_t acc_vec4;    // its length in float4
   int64_t os[4], dos[4];
   int Hq, Sq, Sq_pad, D;
   int64_t rows;  // B*Hq*Sq_pad
@@ -468,38 +491,42 @@ struct PrepArgs {
 
 template <bool BF16>
 __global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= a.rows) return;
-  const int64_t bh = row / a.Sq_pad;
-  const int q = (int)(row % a.Sq_pad);
-  if (q >= a.Sq) {
-    if (lane == 0) {
-      a.lse2[row] = INFINITY;
-      a.delta[row] = 0.f;
-    }
-    return;
-  }
-  const int64_t b = bh / a.Hq, h = bh % a.Hq;
-  const uint16_t* orow = a.o + b * a.os[0] + h * a.os[1] + (int64_t)q * a.os[2];
-  const uint16_t* drow = a.dout + b * a.dos[0] + h * a.dos[1] + (int64_t)q * a.dos[2];
-  float acc = 0.f;
-  for (int d = lane * 4; d < a.D; d += 128) {
-    const uint2 ov = *reinterpret_cast<const uint2*>(orow + d);
-    const uint2 dv = *reinterpret_cast<const uint2*>(drow + d);
-    const float2 o0 = kf::unpack2<BF16>(ov.x), o1 = kf::unpack2<BF16>(ov.y);
-    const float2 d0 = kf::unpack2<BF16>(dv.x), d1 = kf::unpack2<BF16>(dv.y);
-    acc += o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
-  }
+  const int sub = threadIdx.x & 15;
+  const int64_t stride = (int64_t)gridDim.x * 16;
+  for (int64_t row = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4); row - (threadIdx.x >> 4) < a.rows;
+       row += stride) {
+    // every thread of a warp reaches the shuffles below, rows past the end included
+    const bool in = row < a.rows;
+    const int64_t bh = in ? row / a.Sq_pad : 0;
+    const int q = in ? (int)(row % a.Sq_pad) : 0;
+    const bool real = in && q < a.Sq;
+    float acc = 0.f;
+    if (real && sub * 8 < a.D) {
+      const int64_t b = bh / a.Hq, h = bh % a.Hq;
+      const uint4 ov = *reinterpret_cast<const uint4*>(a.o + b * a.os[0] + h * a.os[1] + (int64_t)q * a.os[2] + sub * 8);
+      const uint4 dv = *reinterpret_cast<const uint4*>(a.dout + b * a.dos[0] + h * a.dos[1] + (int64_t)q * a.dos[2] + sub * 8);
+      const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    a.delta[row] = acc;
-    a.lse2[row] = a.lse[bh * a.Sq + q] * kLog2e;
+      for (int j = 0; j < 4; ++j) {
+        const float2 o2 = kf::unpack2<BF16>(ow[j]), d2 = kf::unpack2<BF16>(dw[j]);
+        acc += o2.x * d2.x + o2.y * d2.y;
+      }
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (in && sub == 0) {
+      a.delta[row] = real ? acc : 0.f;
+      a.lse2[row] = real ? a.lse[bh * a.Sq + q] * kLog2e : INFINITY;
+    }
   }
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < a.acc_vec4; i += (int64_t)gridDim.x * 256)
+    a.acc[i] = z;
 }
 
-// dQ = scale * workspace ([bh][qb][D][64] fp32) -> dq [B,Hq,Sq,D] in the input dtype.
+// dQ = scale * workspace ([bh][qb][D][64] fp32) -> dq [B,Hq,Sq,D] in the input
+// dtype: one block per 64-row tile, transposed through shared memory, written
+// with 16-byte row-contiguous stores.
 struct FinishArgs {
   const float* acc;
   uint16_t* dq;
@@ -510,19 +537,29 @@ struct FinishArgs {
 
 template <bool BF16>
 __global__ void __launch_bounds__(256) finish_kernel(const FinishArgs a) {
-  __shared__ float tile[128][kBM + 1];
+  __shared__ float tile[kBM][128 + 1];  // [query][d]
   const int qb = blockIdx.x, bh = blockIdx.y;
-  const float* src = a.acc + ((int64_t)bh * a.nqb + qb) * a.D * kBM;
-  for (int idx = threadIdx.x; idx < a.D * kBM; idx += 256) tile[idx / kBM][idx % kBM] = src[idx];
+  const float4* src = reinterpret_cast<const float4*>(a.acc + ((int64_t)bh * a.nqb + qb) * a.D * kBM);
+  for (int idx = threadIdx.x; idx < a.D * (kBM / 4); idx += 256) {
+    const int d = idx / (kBM / 4), q4 = (idx % (kBM / 4)) * 4;
+    const float4 v = src[idx];
+    tile[q4 + 0][d] = v.x;
+    tile[q4 + 1][d] = v.y;
+    tile[q4 + 2][d] = v.z;
+    tile[q4 + 3][d] = v.w;
+  }
   __syncthreads();
   const int b = bh / a.Hq, h = bh % a.Hq;
-  const int dv = a.D / 2;
-  for (int idx = threadIdx.x; idx < kBM * dv; idx += 256) {
-    const int r = idx / dv, d2 = (idx % dv) * 2;
+  const int nd8 = a.D / 8;
+  for (int idx = threadIdx.x; idx < kBM * nd8; idx += 256) {
+    const int r = idx / nd8, d8 = (idx % nd8) * 8;
     const int q = qb * kBM + r;
     if (q >= a.Sq) continue;
-    uint16_t* dst = a.dq + b * a.qs[0] + (int64_t)h * a.qs[1] + (int64_t)q * a.qs[2] + d2;
-    *reinterpret_cast<uint32_t*>(dst) = kf::pack2<BF16>(tile[d2][r] * a.scale, tile[d2 + 1][r] * a.scale);
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = kf::pack2<BF16>(tile[r][d8 + 2 * j] * a.scale, tile[r][d8 + 2 * j + 1] * a.scale);
+    *reinterpret_cast<uint4*>(a.dq + b * a.qs[0] + (int64_t)h * a.qs[1] + (int64_t)q * a.qs[2] + d8) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -583,9 +620,6 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   const size_t row_bytes = align256((size_t)B * Hq * Sq_pad * 4);
   float* delta = reinterpret_cast<float*>(ws + acc_bytes + row_bytes);
 
-  if (cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * nqb * D * kBM * 4, st) != cudaSuccess)
-    return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: memset of the dQ workspace failed");
-
   PrepArgs pa;
   pa.o = static_cast<const uint16_t*>(o->ptr);
   pa.dout = static_cast<const uint16_t*>(dout->ptr);
@@ -601,7 +635,10 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   pa.Sq_pad = Sq_pad;
   pa.D = D;
   pa.rows = (int64_t)B * Hq * Sq_pad;
-  prep_kernel<BF16><<<(unsigned)((pa.rows + 7) / 8), 256, 0, st>>>(pa);
+  pa.acc = reinterpret_cast<float4*>(dq_acc);
+  pa.acc_vec4 = (int64_t)B * Hq * nqb * D * kBM / 4;
+  const int64_t prep_blocks = std::min<int64_t>((pa.rows + 15) / 16, (int64_t)kf::sm_count_current_device() * 8);
+  prep_kernel<BF16><<<(unsigned)std::max<int64_t>(prep_blocks, 1), 256, 0, st>>>(pa);
   int rc = kf::check_launch("kf_attn_bwd prep");
   if (rc) return rc;
 
