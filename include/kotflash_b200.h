@@ -139,7 +139,8 @@ int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4
  * B*Hq*Sq in [b][h][s] order.  Writes o (rows x D, dtype, contiguous) and,
  * if lse != NULL, the merged LSE.  Empty partials carry LSE = -inf and
  * contribute nothing; a row whose partials are all empty yields O = 0 and
- * LSE = -inf.  Used for the cross-GPU merge after the all-gather. */
+ * LSE = -inf.  1 <= num_splits <= 512 (KF_ERR_UNSUPPORTED above).  Used for
+ * the cross-GPU merge after the all-gather. */
 int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits,
                       int64_t rows, int64_t D, void* o, float* lse, int dtype,
                       void* stream);

@@ -22,6 +22,8 @@
 //    (O normalised, LSE natural log) that the merge kernel combines.
 #include <math.h>
 
+#include <utility>
+
 #include "kf_host.h"
 #include "kf_sm100.cuh"
 
@@ -109,7 +111,15 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     }
     kf::fence_barrier_init();
     abort_any = 0;
+    kf::tma_prefetch_desc(&map_k);
+    kf::tma_prefetch_desc(&map_v);
   }
+  // Launched with programmatic stream serialization: everything above ran
+  // while the previous kernel of the stream may still be finishing; nothing
+  // below may start before it has completed.  The merge kernel that follows
+  // may be scheduled from here on (it waits for this grid the same way).
+  kf::griddep_wait();
+  kf::griddep_launch_dependents();
   __syncthreads();
   int issued = 0;  // tiles whose loads thread 0 has issued
   // one thread streams K/V tiles (TMA, no multicast); the ring is recycled
@@ -125,8 +135,6 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     }
   };
   if (tid == 0) {
-    kf::tma_prefetch_desc(&map_k);
-    kf::tma_prefetch_desc(&map_v);
     for (int t = 0; t < STAGES && t < n_tiles; ++t) issue(t);
     issued = min(STAGES, n_tiles);
   }
@@ -369,7 +377,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   }
 }
 
-// K3b: one warp per output row merges S partials by their LSE weights.
+// K3b: merge of S split partials by their LSE weights.
 struct MergeArgs {
   const float* part_o;
   const float* part_lse;
@@ -382,67 +390,95 @@ struct MergeArgs {
   int64_t os0, os1, os2;
 };
 
-// One 128-thread block per output row.  Warp 0 turns the row's S partial LSEs
-// into normalised weights in shared memory; then thread (chunk c, group g)
-// accumulates 4 columns over splits g, g + G, g + 2G, ... (G = 128 / (D/4)
-// groups), all loads independent, and the G partial sums are reduced through
-// shared memory.  Few dependent rounds even with hundreds of splits.
+// One 256-thread block per output row, built to need one round trip to L2:
+// every thread first issues the loads of its partial-O chunks (thread (c, g)
+// owns 4 columns c of splits g, g + G, ... with G = 256 / (D/4)), then the
+// block reduces the partial LSEs (max, then the sum of weights) while those
+// loads are in flight, and finally accumulates and reduces the G groups
+// through shared memory.
+constexpr int kMergeThreads = 256;
+constexpr int kMergeBatch = 8;  // partial loads in flight per thread
+
 template <bool BF16>
-__global__ void __launch_bounds__(128) merge_kernel(const MergeArgs a) {
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeArgs a) {
   extern __shared__ float sm[];          // [S] weights, then [G][D] partial sums
   float* wts = sm;
   float* part = sm + ((a.S + 3) & ~3);
-  __shared__ float row_lse;
-  const int tid = threadIdx.x, lane = tid & 31;
+  __shared__ float red[kMergeThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = blockIdx.x;
-  if (tid < 32) {
-    float mx = -INFINITY;
-    for (int s = lane; s < a.S; s += 32) mx = fmaxf(mx, a.part_lse[(int64_t)s * a.rows + row]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float den = 0.f;
-    for (int s = lane; s < a.S; s += 32) {
-      const float ls = a.part_lse[(int64_t)s * a.rows + row];
-      const float w = (mx == -INFINITY || ls == -INFINITY) ? 0.f : kf::ex2((ls - mx) * kLog2e);
-      wts[s] = w;
-      den += w;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    __syncwarp();
-    for (int s = lane; s < a.S; s += 32) wts[s] *= inv;
-    if (lane == 0) row_lse = den > 0.f ? mx + logf(den) : -INFINITY;
-  }
-  __syncthreads();
   const int tpr = a.D / 4;               // threads per split (one 4-column chunk each)
-  const int groups = 128 / tpr;
+  const int groups = kMergeThreads / tpr;
   const int c = tid % tpr, g = tid / tpr;
+  const float* src = a.part_o + row * a.D + c * 4;
+  const int64_t sstride = a.rows * a.D;
+  kf::griddep_wait();  // partials of the split kernel (launched as its programmatic dependent)
+
+  float4 pb[kMergeBatch];
+#pragma unroll
+  for (int u = 0; u < kMergeBatch; ++u) {
+    const int s = g + u * groups;
+    pb[u] = s < a.S ? *reinterpret_cast<const float4*>(src + (int64_t)s * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // partial LSEs: S <= 2 * kMergeThreads
+  float ls[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int s = tid + u * kMergeThreads;
+    ls[u] = s < a.S ? a.part_lse[(int64_t)s * a.rows + row] : -INFINITY;
+  }
+  float mx = fmaxf(ls[0], ls[1]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kMergeThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  float den = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int s = tid + u * kMergeThreads;
+    const float w = (mx == -INFINITY || ls[u] == -INFINITY) ? 0.f : kf::ex2((ls[u] - mx) * kLog2e);
+    if (s < a.S) wts[s] = w;
+    den += w;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  __syncthreads();  // red[] reads done, wts[] written
+  if (lane == 0) red[warp] = den;
+  __syncthreads();
+  den = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMergeThreads / 32; ++w) den += red[w];
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+
   if (g < groups) {
-    const float* src = a.part_o + row * a.D + c * 4;
-    const int64_t sstride = a.rows * a.D;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int s = g;
-    for (; s + 3 * groups < a.S; s += 4 * groups) {
-      float4 p[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) p[u] = *reinterpret_cast<const float4*>(src + (int64_t)(s + u * groups) * sstride);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float w = wts[s + u * groups];
-        acc[0] += w * p[u].x;
-        acc[1] += w * p[u].y;
-        acc[2] += w * p[u].z;
-        acc[3] += w * p[u].w;
-      }
+    for (int u = 0; u < kMergeBatch; ++u) {
+      const int s = g + u * groups;
+      const float w = s < a.S ? wts[s] : 0.f;
+      acc[0] += w * pb[u].x;
+      acc[1] += w * pb[u].y;
+      acc[2] += w * pb[u].z;
+      acc[3] += w * pb[u].w;
     }
-    for (; s < a.S; s += groups) {
-      const float w = wts[s];
-      const float4 p = *reinterpret_cast<const float4*>(src + (int64_t)s * sstride);
-      acc[0] += w * p.x;
-      acc[1] += w * p.y;
-      acc[2] += w * p.z;
-      acc[3] += w * p.w;
+    for (int s0 = g + kMergeBatch * groups; s0 < a.S; s0 += kMergeBatch * groups) {
+#pragma unroll
+      for (int u = 0; u < kMergeBatch; ++u) {
+        const int s = s0 + u * groups;
+        pb[u] = s < a.S ? *reinterpret_cast<const float4*>(src + (int64_t)s * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kMergeBatch; ++u) {
+        const int s = s0 + u * groups;
+        const float w = s < a.S ? wts[s] : 0.f;
+        acc[0] += w * pb[u].x;
+        acc[1] += w * pb[u].y;
+        acc[2] += w * pb[u].z;
+        acc[3] += w * pb[u].w;
+      }
     }
     *reinterpret_cast<float4*>(part + g * a.D + c * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
@@ -460,22 +496,45 @@ __global__ void __launch_bounds__(128) merge_kernel(const MergeArgs a) {
     const int64_t s_ = row % a.Sq;
     const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
     uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + tid * 4;
-    const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
+    const uint32_t lo = kf::pack2<BF16>(acc[0] * inv, acc[1] * inv), hi = kf::pack2<BF16>(acc[2] * inv, acc[3] * inv);
     *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-    if (tid == 0 && a.lse) a.lse[row] = row_lse;
+    if (tid == 0 && a.lse) a.lse[row] = den > 0.f ? mx + logf(den) : -INFINITY;
   }
+}
+
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// before the previous kernel in the stream finishes and orders itself with
+// griddepcontrol.wait, hiding launch latency between back-to-back kernels
+// (split -> merge, and one decode step -> the next).
+template <typename... KArgs, typename... Args>
+int launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kf::set_error(KF_ERR_CUDA, "%s: launch failed", what);
+  }
+  return kf::check_launch(what);
 }
 
 template <bool BF16>
 int launch_merge(const MergeArgs& m, cudaStream_t st) {
-  const int groups = 128 / (m.D / 4);
+  const int groups = kMergeThreads / (m.D / 4);
   const size_t smem = (size_t)(((m.S + 3) & ~3) + groups * m.D) * sizeof(float);
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(merge_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf merge: cannot reserve %zu bytes of shared memory", smem);
   if (m.rows > 0x7fffffffLL) return kf::set_error(KF_ERR_UNSUPPORTED, "kf merge: too many rows");
-  merge_kernel<BF16><<<(unsigned)m.rows, 128, smem, st>>>(m);
-  return kf::check_launch("kf merge");
+  return launch_dependent(merge_kernel<BF16>, dim3((unsigned)m.rows), dim3(kMergeThreads), smem, st, "kf merge", m);
 }
 
 template <bool BF16, int NP, int MT>
@@ -491,8 +550,7 @@ int launch_split(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& 
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
   dim3 grid(a.num_splits, a.B * a.Hkv, row_blocks);
-  kern<<<grid, kThreads, smem, st>>>(mk, mv, a);
-  return kf::check_launch("kf_decode");
+  return launch_dependent(kern, grid, dim3(kThreads), smem, st, "kf_decode", mk, mv, a);
 }
 
 template <bool BF16>
@@ -668,6 +726,8 @@ extern "C" int kf_merge_partials(const float* part_o, const float* part_lse, int
   if (!part_o || !part_lse || !o) return set_error(KF_ERR_INVALID, "kf_merge_partials: null pointer");
   if (num_splits <= 0 || rows <= 0 || D <= 0 || D > 128 || D % 4 != 0)
     return set_error(KF_ERR_INVALID, "kf_merge_partials: need splits > 0, rows > 0, D % 4 == 0, D <= 128");
+  if (num_splits > 2 * kMergeThreads)
+    return set_error(KF_ERR_UNSUPPORTED, "kf_merge_partials: at most %d splits", 2 * kMergeThreads);
   if (dtype != KF_F16 && dtype != KF_BF16)
     return set_error(KF_ERR_INVALID, "kf_merge_partials: dtype must be fp16 or bf16");
   if ((reinterpret_cast<uintptr_t>(part_o) & 15) || (reinterpret_cast<uintptr_t>(o) & 7))

@@ -98,6 +98,14 @@ KF_DEVI uint64_t exp2_poly2(float x0, float x1) {
   return r;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still running; it must call
+// griddep_wait() before touching any memory that kernel writes.
+// griddep_launch_dependents() lets the next such kernel be scheduled early.
+KF_DEVI void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+KF_DEVI void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Wait budget for every device-side spin: about one second of wall time.
 constexpr uint64_t kWaitBudgetNs = 1000000000ull;
 
