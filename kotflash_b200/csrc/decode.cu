@@ -77,12 +77,20 @@ constexpr int kTileN = kWarps * kTileKeys;  // 64 keys per TMA tile
 
 // NP = 64-column panels of the padded head dim (1 or 2), MT = 16-row m-tiles of
 // packed query rows, STAGES = depth of the K/V ring.
-template <bool BF16, int NP, int MT, int STAGES>
+//
+// N8 (at most 8 packed rows, e.g. one query token of a 4-way GQA group): the
+// products are taken transposed, S^T = K Q^T and O^T = V^T P^T, so the query
+// rows sit on the MMA's n = 8 side instead of padding a 16-row m tile.  That
+// halves the MMAs per key (the legacy warp MMA is what bounds this kernel at
+// small row counts).  P^T goes from the S^T accumulator layout to the B
+// operand layout with movmatrix (8x8 transposes in registers); the row max
+// and sum reduce across the 8 lane groups that hold a row's keys.
+template <bool BF16, int NP, int MT, int STAGES, bool N8>
 __global__ void __launch_bounds__(kThreads)
 decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                     const DecodeArgs a) {
   constexpr int DP = NP * 64;
-  constexpr int ROWS = MT * 16;
+  constexpr int ROWS = N8 ? 8 : MT * 16;
   constexpr int Q_ROW_BYTES = DP * 2;
   constexpr int CHUNKS = DP / 8;                 // 16-byte chunks per row
   constexpr int PANEL = kTileN * 128;            // one 64-column panel of a tile
@@ -174,6 +182,24 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   }
   const uint32_t sQ_u = kf::smem_u32(sQ);
   const int wr0 = warp * kTileKeys;   // this warp's 16 rows of every tile
+  // N8 state: Q^T as B fragments (k = head dim, n = row), running max / sum
+  // of rows 2 (lane % 4) + {0, 1}, and O^T accumulators (m = head dim).
+  uint32_t qb[DP / 16][2];
+  float m8[2] = {-INFINITY, -INFINITY}, l8[2] = {0.f, 0.f};
+  float ot[DP / 16][4];
+  if constexpr (N8) {
+#pragma unroll
+    for (int kk = 0; kk < DP / 16; kk += 2) {
+      uint32_t r4[4];
+      kf::ldmatrix_x4(r4, sQ_u + swz(lane & 7, 2 * kk + (lane >> 3), Q_ROW_BYTES));
+      qb[kk][0] = r4[0];
+      qb[kk][1] = r4[1];
+      qb[kk + 1][0] = r4[2];
+      qb[kk + 1][1] = r4[3];
+    }
+#pragma unroll
+    for (int dm = 0; dm < DP / 16; ++dm) ot[dm][0] = ot[dm][1] = ot[dm][2] = ot[dm][3] = 0.f;
+  }
   bool ok = true;
   int t_stop = n_tiles;
   for (int t = 0; t < n_tiles; ++t) {
@@ -212,64 +238,119 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     }
     const uint32_t sk_u = kf::smem_u32(kt), sv_u = kf::smem_u32(vt);
 
-    // S = Q K^T for this warp's 16 keys
-    float sc[MT][2][4];
+    if constexpr (N8) {
+      // S^T (16 keys x 8 rows) = K Q^T
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int n = 0; n < 2; ++n) sc[mt][n][0] = sc[mt][n][1] = sc[mt][n][2] = sc[mt][n][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < DP / 16; ++kk) {
-      uint32_t kb[4];
-      kf::ldmatrix_x4(kb, sk_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), kTileN));
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        uint32_t qa[4];
-        kf::ldmatrix_x4(qa, sQ_u + swz(mt * 16 + (lane & 15), 2 * kk + (lane >> 4), Q_ROW_BYTES));
-        kf::mma_16816<BF16>(sc[mt][0], qa, kb[0], kb[1]);
-        kf::mma_16816<BF16>(sc[mt][1], qa, kb[2], kb[3]);
+      for (int kk = 0; kk < DP / 16; ++kk) {
+        uint32_t ka[4];
+        kf::ldmatrix_x4(ka, sk_u + tma_swz(wr0 + (lane & 15), 2 * kk + (lane >> 4), kTileN));
+        kf::mma_16816<BF16>(c, ka, qb[kk][0], qb[kk][1]);
       }
-    }
-
-    // online softmax (log2 domain), then O += P V
+      // rows 2 (lane % 4) + {0, 1}; keys lane / 4 (c0, c1) and lane / 4 + 8 (c2, c3)
+      const int ka0 = key0 + (lane >> 2);
+      float x[4];
+      x[0] = ka0 < key_end ? c[0] * a.scale_log2 : -INFINITY;
+      x[1] = ka0 < key_end ? c[1] * a.scale_log2 : -INFINITY;
+      x[2] = ka0 + 8 < key_end ? c[2] * a.scale_log2 : -INFINITY;
+      x[3] = ka0 + 8 < key_end ? c[3] * a.scale_log2 : -INFINITY;
+      float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      uint32_t pa[4];
+      for (int off = 4; off < 32; off <<= 1) {
+        mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], off));
+        mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], off));
+      }
+      float alpha[2], mu[2];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float x[4];
+      for (int j = 0; j < 2; ++j) {
+        const float m_new = fmaxf(m8[j], mx[j]);
+        mu[j] = m_new == -INFINITY ? 0.f : m_new;
+        alpha[j] = kf::ex2(m8[j] - mu[j]);
+        m8[j] = m_new;
+      }
+      const float p0 = kf::ex2(x[0] - mu[0]), p1 = kf::ex2(x[1] - mu[1]);
+      const float p2 = kf::ex2(x[2] - mu[0]), p3 = kf::ex2(x[3] - mu[1]);
+      l8[0] = l8[0] * alpha[0] + (p0 + p2);
+      l8[1] = l8[1] * alpha[1] + (p1 + p3);
+      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int key = key0 + n * 8 + 2 * (lane & 3) + e;
-            x[n * 2 + e] = key < key_end ? sc[mt][n][half * 2 + e] * a.scale_log2 : -INFINITY;
-          }
-        const float mx = warp_max4(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
-        const float m_new = fmaxf(m_run[mt][half], mx);
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = kf::ex2(m_run[mt][half] - m_use);
-        float p[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) p[j] = kf::ex2(x[j] - m_use);
-        l_run[mt][half] = l_run[mt][half] * alpha + (p[0] + p[1] + p[2] + p[3]);
-        m_run[mt][half] = m_new;
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // skip when no row max moved
-#pragma unroll
-          for (int n = 0; n < DP / 8; ++n) {
-            o_acc[mt][n][half * 2 + 0] *= alpha;
-            o_acc[mt][n][half * 2 + 1] *= alpha;
-          }
+        for (int dm = 0; dm < DP / 16; ++dm) {
+          ot[dm][0] *= alpha[0];
+          ot[dm][1] *= alpha[1];
+          ot[dm][2] *= alpha[0];
+          ot[dm][3] *= alpha[1];
         }
-        pa[half] = kf::pack2<BF16>(p[0], p[1]);      // keys 0-7 of the warp's 16
-        pa[2 + half] = kf::pack2<BF16>(p[2], p[3]);  // keys 8-15
       }
+      // P^T as the B operand (k = key, n = row): transpose the two 8x8 halves
+      const uint32_t pb0 = kf::movmatrix_trans(kf::pack2<BF16>(p0, p1));
+      const uint32_t pb1 = kf::movmatrix_trans(kf::pack2<BF16>(p2, p3));
+      // O^T (head dim x 8 rows) += V^T P^T
 #pragma unroll
-      for (int dn = 0; dn < DP / 16; ++dn) {
-        uint32_t vb[4];
-        kf::ldmatrix_x4_trans(vb, sv_u + tma_swz(wr0 + (lane & 15), 2 * dn + (lane >> 4), kTileN));
-        kf::mma_16816<BF16>(o_acc[mt][2 * dn], pa, vb[0], vb[1]);
-        kf::mma_16816<BF16>(o_acc[mt][2 * dn + 1], pa, vb[2], vb[3]);
+      for (int dm = 0; dm < DP / 16; ++dm) {
+        uint32_t va[4];
+        kf::ldmatrix_x4_trans(va, sv_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * dm + ((lane >> 3) & 1), kTileN));
+        kf::mma_16816<BF16>(ot[dm], va, pb0, pb1);
+      }
+    } else {
+      // S = Q K^T for this warp's 16 keys
+      float sc[MT][2][4];
+  #pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+  #pragma unroll
+        for (int n = 0; n < 2; ++n) sc[mt][n][0] = sc[mt][n][1] = sc[mt][n][2] = sc[mt][n][3] = 0.f;
+  #pragma unroll
+      for (int kk = 0; kk < DP / 16; ++kk) {
+        uint32_t kb[4];
+        kf::ldmatrix_x4(kb, sk_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), kTileN));
+  #pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t qa[4];
+          kf::ldmatrix_x4(qa, sQ_u + swz(mt * 16 + (lane & 15), 2 * kk + (lane >> 4), Q_ROW_BYTES));
+          kf::mma_16816<BF16>(sc[mt][0], qa, kb[0], kb[1]);
+          kf::mma_16816<BF16>(sc[mt][1], qa, kb[2], kb[3]);
+        }
+      }
+
+      // online softmax (log2 domain), then O += P V
+  #pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t pa[4];
+  #pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float x[4];
+  #pragma unroll
+          for (int n = 0; n < 2; ++n)
+  #pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = key0 + n * 8 + 2 * (lane & 3) + e;
+              x[n * 2 + e] = key < key_end ? sc[mt][n][half * 2 + e] * a.scale_log2 : -INFINITY;
+            }
+          const float mx = warp_max4(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
+          const float m_new = fmaxf(m_run[mt][half], mx);
+          const float m_use = m_new == -INFINITY ? 0.f : m_new;
+          const float alpha = kf::ex2(m_run[mt][half] - m_use);
+          float p[4];
+  #pragma unroll
+          for (int j = 0; j < 4; ++j) p[j] = kf::ex2(x[j] - m_use);
+          l_run[mt][half] = l_run[mt][half] * alpha + (p[0] + p[1] + p[2] + p[3]);
+          m_run[mt][half] = m_new;
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {  // skip when no row max moved
+  #pragma unroll
+            for (int n = 0; n < DP / 8; ++n) {
+              o_acc[mt][n][half * 2 + 0] *= alpha;
+              o_acc[mt][n][half * 2 + 1] *= alpha;
+            }
+          }
+          pa[half] = kf::pack2<BF16>(p[0], p[1]);      // keys 0-7 of the warp's 16
+          pa[2 + half] = kf::pack2<BF16>(p[2], p[3]);  // keys 8-15
+        }
+  #pragma unroll
+        for (int dn = 0; dn < DP / 16; ++dn) {
+          uint32_t vb[4];
+          kf::ldmatrix_x4_trans(vb, sv_u + tma_swz(wr0 + (lane & 15), 2 * dn + (lane >> 4), kTileN));
+          kf::mma_16816<BF16>(o_acc[mt][2 * dn], pa, vb[0], vb[1]);
+          kf::mma_16816<BF16>(o_acc[mt][2 * dn + 1], pa, vb[2], vb[3]);
+        }
       }
     }
     __syncwarp();
@@ -277,15 +358,22 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   }
 
   // ---- merge the 4 warps in shared memory (reuses the ring: all tiles consumed)
+  if constexpr (N8) {
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float l = l_run[mt][half];
-      l += __shfl_xor_sync(0xffffffffu, l, 1);
-      l += __shfl_xor_sync(0xffffffffu, l, 2);
-      l_run[mt][half] = l;
-    }
+      for (int off = 4; off < 32; off <<= 1) l8[j] += __shfl_xor_sync(0xffffffffu, l8[j], off);
+  } else {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float l = l_run[mt][half];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        l_run[mt][half] = l;
+      }
+  }
   __syncthreads();
   if (abort_any) {
     // a bounded wait expired: let the loads already in flight land (bounded),
@@ -310,22 +398,39 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   float* row_w = ml + kWarps * ROWS * 2;               // [warp][ROWS] weights
   float* row_lse = row_w + kWarps * ROWS;              // [ROWS]
   float* obuf = row_lse + ROWS;                        // [warp][ROWS][DP]
+  if constexpr (N8) {
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = mt * 16 + (lane >> 2) + half * 8;
-      if ((lane & 3) == 0) {
-        ml[(warp * ROWS + r) * 2 + 0] = m_run[mt][half];
-        ml[(warp * ROWS + r) * 2 + 1] = l_run[mt][half];
+    for (int j = 0; j < 2; ++j) {
+      const int r = 2 * (lane & 3) + j;
+      if (lane < 4) {
+        ml[(warp * ROWS + r) * 2 + 0] = m8[j];
+        ml[(warp * ROWS + r) * 2 + 1] = l8[j];
       }
 #pragma unroll
-      for (int n = 0; n < DP / 8; ++n) {
-        const int c = n * 8 + 2 * (lane & 3);
-        obuf[(warp * ROWS + r) * DP + c] = o_acc[mt][n][half * 2];
-        obuf[(warp * ROWS + r) * DP + c + 1] = o_acc[mt][n][half * 2 + 1];
+      for (int dm = 0; dm < DP / 16; ++dm) {
+        const int d = dm * 16 + (lane >> 2);
+        obuf[(warp * ROWS + r) * DP + d] = ot[dm][j];
+        obuf[(warp * ROWS + r) * DP + d + 8] = ot[dm][2 + j];
       }
     }
+  } else {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = mt * 16 + (lane >> 2) + half * 8;
+        if ((lane & 3) == 0) {
+          ml[(warp * ROWS + r) * 2 + 0] = m_run[mt][half];
+          ml[(warp * ROWS + r) * 2 + 1] = l_run[mt][half];
+        }
+#pragma unroll
+        for (int n = 0; n < DP / 8; ++n) {
+          const int c = n * 8 + 2 * (lane & 3);
+          obuf[(warp * ROWS + r) * DP + c] = o_acc[mt][n][half * 2];
+          obuf[(warp * ROWS + r) * DP + c + 1] = o_acc[mt][n][half * 2 + 1];
+        }
+      }
+  }
   __syncthreads();
   if (tid < ROWS) {
     float M = -INFINITY;
@@ -537,16 +642,16 @@ int launch_merge(const MergeArgs& m, cudaStream_t st) {
   return launch_dependent(merge_kernel<BF16>, dim3((unsigned)m.rows), dim3(kMergeThreads), smem, st, "kf merge", m);
 }
 
-template <bool BF16, int NP, int MT>
+template <bool BF16, int NP, int MT, bool N8 = false>
 int launch_split(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int row_blocks,
                  cudaStream_t st) {
   constexpr int STAGES = NP == 1 ? 4 : 2;
   constexpr int DP = NP * 64;
-  constexpr int ROWS = MT * 16;
+  constexpr int ROWS = N8 ? 8 : MT * 16;
   const size_t pipe = 1024 + (size_t)STAGES * 2 * NP * kTileN * 128 + (size_t)ROWS * DP * 2;
   const size_t merge = 1024 + (size_t)kWarps * ROWS * 3 * 4 + ROWS * 4 + (size_t)kWarps * ROWS * DP * 4;
   const size_t smem = pipe > merge ? pipe : merge;
-  auto kern = decode_split_kernel<BF16, NP, MT, STAGES>;
+  auto kern = decode_split_kernel<BF16, NP, MT, STAGES, N8>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
   dim3 grid(a.num_splits, a.B * a.Hkv, row_blocks);
@@ -560,6 +665,9 @@ int dispatch_split(const DecodeArgs& a, const kf_tensor4* k, const kf_tensor4* v
   if ((rc = kf::encode_tmap_4d(&mk, k, 64, kTileN))) return rc;
   if ((rc = kf::encode_tmap_4d(&mv, v, 64, kTileN))) return rc;
   const int np = a.D <= 64 ? 1 : 2;
+  if (a.rows <= 8)  // transposed products: rows on the n = 8 side
+    return np == 1 ? launch_split<BF16, 1, 1, true>(a, mk, mv, 1, st)
+                   : launch_split<BF16, 2, 1, true>(a, mk, mv, 1, st);
   const int mt_max = np == 1 ? 4 : 2;
   int mt = (a.rows + 15) / 16;
   if (mt > mt_max) mt = mt_max;

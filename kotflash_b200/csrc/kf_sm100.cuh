@@ -394,6 +394,14 @@ KF_DEVI void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
                : "r"(saddr));
 }
 
+// Transpose of an 8x8 matrix of 16-bit elements held as one register per
+// lane (lane l: row l / 4, columns 2 (l % 4) + {0, 1}).
+KF_DEVI uint32_t movmatrix_trans(uint32_t v) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(v));
+  return r;
+}
+
 template <bool BF16>
 KF_DEVI void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   if constexpr (BF16) {
