@@ -238,37 +238,73 @@ def bench_prefill(args, world, rank, local, dtype):
 
 
 def bench_prefill_e2e(args, world, rank, dtype):
-    """Same step with host (pinned) inputs copied in and all outputs copied out."""
-    hq_, hk_, hv_, hdo_ = (t.cpu().pin_memory() for t in make_prefill_inputs(dtype, 99 + rank, "cuda"))
-    dq_h = torch.empty_like(hq_).pin_memory()
-    dk_h = torch.empty_like(hk_).pin_memory()
-    dv_h = torch.empty_like(hv_).pin_memory()
-    o_h = torch.empty_like(hq_).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, hdo_))
-    d2h = sum(t.numel() * t.element_size() for t in (o_h, dq_h, dk_h, dv_h))
+    """Same step with host (pinned) inputs copied in and all outputs copied out.
 
-    def step():
-        q = hq_.to("cuda", non_blocking=True)
-        k = hk_.to("cuda", non_blocking=True)
-        v = hv_.to("cuda", non_blocking=True)
-        do = hdo_.to("cuda", non_blocking=True)
-        out, (dq, dk, dv) = prefill_step(q, k, v, do)
-        o_h.copy_(out.detach(), non_blocking=True)
-        dq_h.copy_(dq, non_blocking=True)
-        dk_h.copy_(dk, non_blocking=True)
-        dv_h.copy_(dv, non_blocking=True)
+    Steps are software-pipelined the way a training loop feeding the GPU from
+    host memory would run them: step i's inputs are copied in on an H2D stream
+    while step i-1 computes, and step i-1's O/dQ/dK/dV are copied out on a D2H
+    stream while step i computes (PCIe moves both directions at once).  Device
+    inputs are double-buffered.  Every step's copies lie inside the timed
+    region: the clock stops after the last step's outputs have reached host
+    memory.
+    """
+    hosts = [tuple(t.cpu().pin_memory() for t in make_prefill_inputs(dtype, 99 + rank + 7 * j, "cuda"))
+             for j in range(2)]
+    outs_h = [tuple(torch.empty_like(t).pin_memory() for t in (hosts[j][0], hosts[j][0], hosts[j][1], hosts[j][2]))
+              for j in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in hosts[0])
+    d2h = sum(t.numel() * t.element_size() for t in outs_h[0])
+    dev = [tuple(torch.empty_like(t, device="cuda") for t in hosts[j]) for j in range(2)]
+    comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+    for j in range(2):
+        in_free[j].record(comp)
+        out_done[j].record(s_out)
 
-    for _ in range(max(1, args.warmup)):
-        step()
+    def copy_in(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(in_free[j])
+            for d, h in zip(dev[j], hosts[j]):
+                d.copy_(h, non_blocking=True)
+            in_ready[j].record(s_in)
+
+    def compute_and_copy_out(i):
+        j = i % 2
+        comp.wait_event(in_ready[j])
+        q, k, v, do = dev[j]
+        out, (dq, dk, dv) = prefill_step(q.detach(), k.detach(), v.detach(), do)
+        in_free[j].record(comp)
+        ready = torch.cuda.Event()
+        ready.record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ready)
+            for h, d in zip(outs_h[j], (out.detach(), dq, dk, dv)):
+                d.record_stream(s_out)
+                h.copy_(d, non_blocking=True)
+            out_done[j].record(s_out)
+
+    def run(n):
+        s_in.wait_stream(comp)  # the first copy starts after the clock does
+        copy_in(0)
+        for i in range(n):
+            if i + 1 < n:
+                copy_in(i + 1)
+            compute_and_copy_out(i)
+        comp.wait_stream(s_out)
+
+    run(max(2, args.warmup))
     torch.cuda.synchronize()
-    steps = max(2, args.steps // 2)
+    steps = max(4, args.steps // 2)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    start.record()
-    for _ in range(steps):
-        step()
-    end.record()
+    start.record(comp)
+    run(steps)
+    end.record(comp)
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
