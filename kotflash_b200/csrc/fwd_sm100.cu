@@ -33,6 +33,8 @@
 // tensor cores at head_dim 128.
 #include <math.h>
 
+#include <algorithm>
+
 #include "kf_host.h"
 #include "kf_sm100.cuh"
 
@@ -57,13 +59,14 @@ struct FwdParams {
   int causal;
   int m_blocks;        // cdiv(Sq, 128)
   int slots_per_kvh;   // G * m_blocks
-  int ctas_per_kvh;    // cdiv(slots_per_kvh, 2)
+  int ctas_per_kvh;    // cdiv(slots_per_kvh, 2): work items per KV head
+  int n_items;         // B * Hkv * ctas_per_kvh
   float scale_log2;
   int32_t* status;
 };
 
 struct __align__(8) FwdBarriers {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
   uint64_t s_full[2], p_full[2];
@@ -99,12 +102,17 @@ struct TileInfo {
   int n_blocks;
 };
 
-__device__ __forceinline__ TileInfo tile_info(const FwdParams& p) {
+// Items are numbered heaviest first across all KV heads (for causal masks the
+// later row blocks see more keys).  The persistent CTAs take them in rounds
+// of gridDim.x items, in forward order on even rounds and reverse order on
+// odd rounds, so a CTA that drew a heavy item in one round draws a light one
+// in the next and the CTAs' totals stay close.
+__device__ __forceinline__ TileInfo tile_info(const FwdParams& p, int item) {
   TileInfo ti;
   const int per_bh = p.ctas_per_kvh;
-  const int bh = blockIdx.x / per_bh;
-  // heavier (later) row blocks first so causal tails do not straggle
-  const int c = per_bh - 1 - (blockIdx.x % per_bh);
+  const int n_bh = p.B * p.Hkv;
+  const int bh = item % n_bh;
+  const int c = per_bh - 1 - item / n_bh;
   ti.b = bh / p.Hkv;
   ti.kvh = bh % p.Hkv;
   int row_end_max = 0;
@@ -123,6 +131,13 @@ __device__ __forceinline__ TileInfo tile_info(const FwdParams& p) {
   return ti;
 }
 
+// Item of round r for this CTA, or -1 when the last round has none for it.
+__device__ __forceinline__ int round_item(int r, int n_items) {
+  const int g = (int)gridDim.x;
+  const int idx = r * g + ((r & 1) ? g - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  return idx < n_items ? idx : -1;
+}
+
 template <bool BF16, int NP, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -138,18 +153,16 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(sV + kStages * TILE);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const TileInfo ti = tile_info(p);
-  const int nblk = ti.n_blocks;
   constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
 
-  const int nt = ti.valid[1] ? 2 : 1;  // Q tiles in use == MMA issuers
   if (tid == 0) {
     kf::mbar_init(&bars->q_full, 1);
+    kf::mbar_init(&bars->q_empty, 2);  // one commit per issuer
     for (int s = 0; s < kStages; ++s) {
       kf::mbar_init(&bars->k_full[s], 1);
-      kf::mbar_init(&bars->k_empty[s], nt);  // one commit per issuer
+      kf::mbar_init(&bars->k_empty[s], 2);
       kf::mbar_init(&bars->v_full[s], 1);
-      kf::mbar_init(&bars->v_empty[s], nt);
+      kf::mbar_init(&bars->v_empty[s], 2);
     }
     for (int t = 0; t < 2; ++t) {
       kf::mbar_init(&bars->s_full[t], 1);
@@ -174,33 +187,51 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   kf::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
+  // Persistent CTA: every role walks the same item sequence (round_item);
+  // barrier phases run on across items (g counts K/V blocks of all items,
+  // it counts items).
+  const int rounds = (p.n_items + (int)gridDim.x - 1) / (int)gridDim.x;
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      kf::mbar_arrive_expect_tx(&bars->q_full, nt * TILE);
-      for (int t = 0; t < nt; ++t)
-        for (int pn = 0; pn < NP; ++pn)
-          kf::tma_load_4d(sQ + t * TILE + pn * PANEL, &map_q, &bars->q_full, pn * 64, ti.row0[t],
-                          ti.head[t], ti.b);
-      for (int j = 0; j < nblk; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = ((j / kStages) & 1) ^ 1;
-        if (!wait_bar(&bars->k_empty[s], ph, bars, p.status)) break;
-        kf::mbar_arrive_expect_tx(&bars->k_full[s], TILE);
-        for (int pn = 0; pn < NP; ++pn)
-          kf::tma_load_4d(sK + s * TILE + pn * PANEL, &map_k, &bars->k_full[s], pn * 64,
-                          j * kBlockN, ti.kvh, ti.b);
-        if (!wait_bar(&bars->v_empty[s], ph, bars, p.status)) break;
-        kf::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
-        for (int pn = 0; pn < NP; ++pn)
-          kf::tma_load_4d(sV + s * TILE + pn * PANEL, &map_v, &bars->v_full[s], pn * 64,
-                          j * kBlockN, ti.kvh, ti.b);
+      int g = 0, it = 0;
+      for (int rd = 0; rd < rounds; ++rd) {
+        const int item = round_item(rd, p.n_items);
+        if (item < 0) continue;
+        const TileInfo ti = tile_info(p, item);
+        const int nt = ti.valid[1] ? 2 : 1;
+        // the previous item's last QK^T has read the Q tiles
+        if (it > 0 && !wait_bar(&bars->q_empty, (it - 1) & 1, bars, p.status)) break;
+        kf::mbar_arrive_expect_tx(&bars->q_full, nt * TILE);
+        for (int t = 0; t < nt; ++t)
+          for (int pn = 0; pn < NP; ++pn)
+            kf::tma_load_4d(sQ + t * TILE + pn * PANEL, &map_q, &bars->q_full, pn * 64, ti.row0[t],
+                            ti.head[t], ti.b);
+        bool ok = true;
+        for (int j = 0; j < ti.n_blocks; ++j) {
+          const int gj = g + j;
+          const int s = gj % kStages;
+          const uint32_t ph = ((gj / kStages) & 1) ^ 1;
+          if (!(ok = wait_bar(&bars->k_empty[s], ph, bars, p.status))) break;
+          kf::mbar_arrive_expect_tx(&bars->k_full[s], TILE);
+          for (int pn = 0; pn < NP; ++pn)
+            kf::tma_load_4d(sK + s * TILE + pn * PANEL, &map_k, &bars->k_full[s], pn * 64,
+                            j * kBlockN, ti.kvh, ti.b);
+          if (!(ok = wait_bar(&bars->v_empty[s], ph, bars, p.status))) break;
+          kf::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
+          for (int pn = 0; pn < NP; ++pn)
+            kf::tma_load_4d(sV + s * TILE + pn * PANEL, &map_v, &bars->v_full[s], pn * 64,
+                            j * kBlockN, ti.kvh, ti.b);
+        }
+        if (!ok) break;
+        g += ti.n_blocks;
+        ++it;
       }
     }
   } else if (warp == 9 || warp == 10) {
     // ------------------------------------------------------------ MMA issuers
     const int t = warp - 9;  // this thread issues every MMA of Q tile t
-    if (lane == 0 && t < nt) {
+    if (lane == 0) {
       const uint32_t idesc_qk = kf::make_idesc_f16(BF16, kBlockM, kBlockN, 0, 0);
       const uint32_t idesc_pv = kf::make_idesc_f16(BF16, kBlockM, d_pad16, 0, 1);
       // Descriptors are built once; each MMA only adds a compile-time offset
@@ -210,48 +241,70 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), PANEL, 1024);
       const uint32_t s_tm = tmem + t * 128, o_tm = tmem + 256 + t * 128;
       // Each GEMM is one straight-line run of MMAs (compile-time trip counts).
-      auto issue_qk = [&](int j) {
-        const uint32_t koff = (j % kStages) * TILE;
+      auto issue_qk = [&](int gj) {
+        const uint32_t koff = (gj % kStages) * TILE;
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
           kf::umma_ss(s_tm, kf::sdesc_at(dq, off), kf::sdesc_at(dk, koff + off), idesc_qk, kk > 0);
         }
       };
-      auto issue_pv = [&](int j) {
-        const uint32_t voff = (j % kStages) * TILE;
+      auto issue_pv = [&](int gj, bool first) {
+        const uint32_t voff = (gj % kStages) * TILE;
 #pragma unroll
         for (int kk = 0; kk < kBlockN / 16; ++kk)
           kf::umma_ts(o_tm, s_tm + kk * 8, kf::sdesc_at(dv, voff + kk * 2048), idesc_pv,
-                      (j > 0 || kk > 0));
+                      (!first || kk > 0));
       };
-      bool ok = wait_bar(&bars->q_full, 0, bars, p.status) &&
-                wait_bar(&bars->k_full[0], 0, bars, p.status);
-      if (ok) {
-        kf::tc_fence_after();
-        issue_qk(0);
-        kf::umma_commit(&bars->s_full[t]);
-        kf::umma_commit(&bars->k_empty[0]);
-      }
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const bool more = j + 1 < nblk;
-        const int s1 = (j + 1) % kStages;
-        const uint32_t ph1 = ((j + 1) / kStages) & 1;
-        if (!(ok = wait_bar(&bars->v_full[s], ph, bars, p.status))) break;
-        if (more && !(ok = wait_bar(&bars->k_full[s1], ph1, bars, p.status))) break;
-        if (!(ok = wait_bar(&bars->p_full[t], j & 1, bars, p.status))) break;
-        kf::tc_fence_after();
-        issue_pv(j);
-        kf::umma_commit(&bars->v_empty[s]);
-        if (more) {
-          issue_qk(j + 1);
+      int g = 0, it = 0, jt = 0;  // K/V blocks (all items), items, blocks of tile t
+      bool ok = true;
+      for (int rd = 0; ok && rd < rounds; ++rd) {
+        const int item = round_item(rd, p.n_items);
+        if (item < 0) continue;
+        const TileInfo ti = tile_info(p, item);
+        const int nt = ti.valid[1] ? 2 : 1;
+        const int nblk = ti.n_blocks;
+        if (t < nt) {
+          // With one Q tile the tile-0 issuer commits twice to the barriers
+          // both issuers release, so their arrival counts stay fixed.
+          const int rel = nt == 2 ? 1 : 2;
+          auto release = [&](uint64_t* bar) {
+            for (int k = 0; k < rel; ++k) kf::umma_commit(bar);
+          };
+          ok = wait_bar(&bars->q_full, it & 1, bars, p.status) &&
+               wait_bar(&bars->k_full[g % kStages], (g / kStages) & 1, bars, p.status);
+          if (!ok) break;
+          kf::tc_fence_after();
+          issue_qk(g);
           kf::umma_commit(&bars->s_full[t]);
-          kf::umma_commit(&bars->k_empty[s1]);
+          if (nblk == 1) release(&bars->q_empty);
+          release(&bars->k_empty[g % kStages]);
+          for (int j = 0; j < nblk; ++j) {
+            const int gj = g + j;
+            const int s = gj % kStages;
+            const uint32_t ph = (gj / kStages) & 1;
+            const bool more = j + 1 < nblk;
+            const int s1 = (gj + 1) % kStages;
+            const uint32_t ph1 = ((gj + 1) / kStages) & 1;
+            if (!(ok = wait_bar(&bars->v_full[s], ph, bars, p.status))) break;
+            if (more && !(ok = wait_bar(&bars->k_full[s1], ph1, bars, p.status))) break;
+            if (!(ok = wait_bar(&bars->p_full[t], (jt + j) & 1, bars, p.status))) break;
+            kf::tc_fence_after();
+            issue_pv(gj, j == 0);
+            release(&bars->v_empty[s]);
+            if (more) {
+              issue_qk(gj + 1);
+              kf::umma_commit(&bars->s_full[t]);
+              if (j + 2 == nblk) release(&bars->q_empty);  // last QK^T of the item
+              release(&bars->k_empty[s1]);
+            }
+          }
+          kf::umma_commit(&bars->o_final[t]);
+          jt += nblk;
         }
+        g += nblk;
+        ++it;
       }
-      kf::umma_commit(&bars->o_final[t]);
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -259,133 +312,147 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t s_col = t * 128, o_col = 256 + t * 128;
-    const int row = ti.row0[t] + r;
-    float m_ref = -INFINITY, l_sum = 0.f;
-    bool ok = ti.valid[t] != 0;
-    for (int j = 0; ok && j < nblk; ++j) {
-      if (!(ok = wait_bar(&bars->s_full[t], j & 1, bars, p.status))) break;
-      kf::tc_fence_after();
-      uint32_t sr[128];
-      kf::tmem_ld32(lane_base + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      kf::tmem_ld32(lane_base + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-      kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
-      kf::tmem_wait_ld();
-      const int key0 = j * kBlockN;
-      const bool need_mask = (key0 + kBlockN > p.Sk) || (p.causal && key0 + kBlockN - 1 > ti.row0[t]);
-      if (need_mask) {
-        const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : kBlockN);
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= lim) sr[c] = 0xFF800000u;  // -inf
-      }
-      // Row max of the raw scores (the scale is positive, so it commutes),
-      // four independent chains of three-input maxima.
-      float mx;
-      {
-        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 128; c += 8) {
-          a0 = kf::fmax3(a0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
-          a1 = kf::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-          a2 = kf::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-          a3 = kf::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-        }
-        mx = kf::fmax3(a0, a1, fmaxf(a2, a3)) * p.scale_log2;
-      }
-      float alpha = 1.f;
-      bool rescale_o = false;
-      if (j == 0) {
-        m_ref = mx;
-      } else if (mx > m_ref + kRescaleThreshold) {
-        alpha = kf::ex2(m_ref - mx);
-        m_ref = mx;
-        rescale_o = true;
-      }
-      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-      l_sum *= alpha;
-      // Tile 0 exponentiates block j after tile 1 finished block j-1, tile 1
-      // after tile 0 finished block j: the two warps sharing each SM
-      // sub-partition never compete for MUFU and issue slots.
-      if (nt == 2 && (t == 1 || j > 0)) {
-        if (!(ok = wait_bar(&bars->turn[t], (t == 1 ? j : j - 1) & 1, bars, p.status))) break;
-      }
-      // P = 2^(s * scale_log2 - m): the argument is one packed fma per pair;
-      // masked blocks (-inf entries) use MUFU only, full blocks send
-      // kPolyPairs of every 8 pairs to the fp32-pipe polynomial.
-      const uint64_t scl = kf::f2(p.scale_log2, p.scale_log2), negm = kf::f2(-m_use, -m_use);
-      uint32_t pk[64];
-      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-      if (need_mask) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          float x0, x1;
-          kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
-          const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
-          acc[c & 3] = kf::add2(acc[c & 3], kf::f2(p0, p1));
-          pk[c] = kf::pack2<BF16>(p0, p1);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          float x0, x1;
-          kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
-          const uint64_t pp = (c & 7) < kPolyPairs ? kf::exp2_poly2(x0, x1) : kf::f2(kf::ex2(x0), kf::ex2(x1));
-          acc[c & 3] = kf::add2(acc[c & 3], pp);
-          float p0, p1;
-          kf::f2_split(pp, p0, p1);
-          pk[c] = kf::pack2<BF16>(p0, p1);
-        }
-      }
-      {
-        float s0, s1;
-        kf::f2_split(kf::add2(kf::add2(acc[0], acc[1]), kf::add2(acc[2], acc[3])), s0, s1);
-        l_sum += s0 + s1;
-      }
-      if (nt == 2) kf::mbar_arrive(&bars->turn[t ^ 1]);
-      kf::tmem_st32(lane_base + s_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-      kf::tmem_st32(lane_base + s_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
-      if (__any_sync(0xffffffffu, rescale_o)) {
-        // O row *= alpha (alpha == 1 on rows that keep their reference max)
-        for (int c0 = 0; c0 < d_pad16; c0 += 32) {
-          uint32_t orow[32];
-          kf::tmem_ld32(lane_base + o_col + c0, orow);
-          kf::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
-          kf::tmem_st32(lane_base + o_col + c0, orow);
-        }
-      }
-      kf::tmem_wait_st();
-      kf::tc_fence_before();
-      kf::mbar_arrive(&bars->p_full[t]);
-    }
-    // ---------------------------------------------------------- epilogue
-    if (ok && wait_bar(&bars->o_final[t], 0, bars, p.status)) {
-      kf::tc_fence_after();
-      const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      const bool row_ok = row < p.Sq;
-      uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)ti.head[t] * p.os[1] + (int64_t)row * p.os[2];
-      for (int c0 = 0; c0 < d_pad16; c0 += 32) {
-        uint32_t ov[32];
-        kf::tmem_ld32(lane_base + o_col + c0, ov);
+    int jt = 0, vt = 0, jturn = 0;  // blocks of tile t, items of tile t, blocks of two-tile items
+    bool ok = true;
+    for (int rd = 0; ok && rd < rounds; ++rd) {
+      const int item = round_item(rd, p.n_items);
+      if (item < 0) continue;
+      const TileInfo ti = tile_info(p, item);
+      const int nt = ti.valid[1] ? 2 : 1;
+      const int nblk = ti.n_blocks;
+      if (!ti.valid[t]) continue;
+      const int row = ti.row0[t] + r;
+      float m_ref = -INFINITY, l_sum = 0.f;
+      for (int j = 0; ok && j < nblk; ++j) {
+        if (!(ok = wait_bar(&bars->s_full[t], (jt + j) & 1, bars, p.status))) break;
+        kf::tc_fence_after();
+        uint32_t sr[128];
+        kf::tmem_ld32(lane_base + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        kf::tmem_ld32(lane_base + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+        kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
         kf::tmem_wait_ld();
-        uint32_t pk[16];
+        const int key0 = j * kBlockN;
+        const bool need_mask = (key0 + kBlockN > p.Sk) || (p.causal && key0 + kBlockN - 1 > ti.row0[t]);
+        if (need_mask) {
+          const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : kBlockN);
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-          pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * inv_l, __uint_as_float(ov[2 * c + 1]) * inv_l);
-        if (row_ok) {
+          for (int c = 0; c < 128; ++c)
+            if (c >= lim) sr[c] = 0xFF800000u;  // -inf
+        }
+        // Row max of the raw scores (the scale is positive, so it commutes),
+        // four independent chains of three-input maxima.
+        float mx;
+        {
+          float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-          for (int g8 = 0; g8 < 4; ++g8) {
-            if (c0 + g8 * 8 < p.D)
-              *reinterpret_cast<uint4*>(orow_g + c0 + g8 * 8) =
-                  make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);
+          for (int c = 0; c < 128; c += 8) {
+            a0 = kf::fmax3(a0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
+            a1 = kf::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+            a2 = kf::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+            a3 = kf::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+          }
+          mx = kf::fmax3(a0, a1, fmaxf(a2, a3)) * p.scale_log2;
+        }
+        float alpha = 1.f;
+        bool rescale_o = false;
+        if (j == 0) {
+          m_ref = mx;
+        } else if (mx > m_ref + kRescaleThreshold) {
+          alpha = kf::ex2(m_ref - mx);
+          m_ref = mx;
+          rescale_o = true;
+        }
+        const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+        l_sum *= alpha;
+        // Tile 0 exponentiates block j after tile 1 finished block j-1, tile 1
+        // after tile 0 finished block j: the two warps sharing each SM
+        // sub-partition never compete for MUFU and issue slots.
+        if (nt == 2 && (t == 1 || j > 0)) {
+          if (!(ok = wait_bar(&bars->turn[t], (jturn + j - (t == 1 ? 0 : 1)) & 1, bars, p.status))) break;
+        }
+        // P = 2^(s * scale_log2 - m): the argument is one packed fma per pair;
+        // masked blocks (-inf entries) use MUFU only, full blocks send
+        // kPolyPairs of every 8 pairs to the fp32-pipe polynomial.
+        const uint64_t scl = kf::f2(p.scale_log2, p.scale_log2), negm = kf::f2(-m_use, -m_use);
+        uint32_t pk[64];
+        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            float x0, x1;
+            kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+            const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
+            acc[c & 3] = kf::add2(acc[c & 3], kf::f2(p0, p1));
+            pk[c] = kf::pack2<BF16>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            float x0, x1;
+            kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+            const uint64_t pp = (c & 7) < kPolyPairs ? kf::exp2_poly2(x0, x1) : kf::f2(kf::ex2(x0), kf::ex2(x1));
+            acc[c & 3] = kf::add2(acc[c & 3], pp);
+            float p0, p1;
+            kf::f2_split(pp, p0, p1);
+            pk[c] = kf::pack2<BF16>(p0, p1);
           }
         }
+        {
+          float s0, s1;
+          kf::f2_split(kf::add2(kf::add2(acc[0], acc[1]), kf::add2(acc[2], acc[3])), s0, s1);
+          l_sum += s0 + s1;
+        }
+        if (nt == 2) kf::mbar_arrive(&bars->turn[t ^ 1]);
+        kf::tmem_st32(lane_base + s_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+        kf::tmem_st32(lane_base + s_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          // O row *= alpha (alpha == 1 on rows that keep their reference max)
+          for (int c0 = 0; c0 < d_pad16; c0 += 32) {
+            uint32_t orow[32];
+            kf::tmem_ld32(lane_base + o_col + c0, orow);
+            kf::tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+            kf::tmem_st32(lane_base + o_col + c0, orow);
+          }
+        }
+        kf::tmem_wait_st();
+        kf::tc_fence_before();
+        kf::mbar_arrive(&bars->p_full[t]);
       }
-      if (row_ok)
-        p.lse[((int64_t)ti.b * p.Hq + ti.head[t]) * p.Sq + row] =
-            l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;
+      // -------------------------------------------------------- epilogue
+      // O is read from TMEM before this thread's next p_full arrival, which
+      // is what lets the next item's first PV overwrite it.
+      if (ok && (ok = wait_bar(&bars->o_final[t], vt & 1, bars, p.status))) {
+        kf::tc_fence_after();
+        const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        const bool row_ok = row < p.Sq;
+        uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)ti.head[t] * p.os[1] + (int64_t)row * p.os[2];
+        for (int c0 = 0; c0 < d_pad16; c0 += 32) {
+          uint32_t ov[32];
+          kf::tmem_ld32(lane_base + o_col + c0, ov);
+          kf::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * inv_l, __uint_as_float(ov[2 * c + 1]) * inv_l);
+          if (row_ok) {
+#pragma unroll
+            for (int g8 = 0; g8 < 4; ++g8) {
+              if (c0 + g8 * 8 < p.D)
+                *reinterpret_cast<uint4*>(orow_g + c0 + g8 * 8) =
+                    make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);
+            }
+          }
+        }
+        if (row_ok)
+          p.lse[((int64_t)ti.b * p.Hq + ti.head[t]) * p.Sq + row] =
+              l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;
+      }
+      jt += nblk;
+      ++vt;
+      if (nt == 2) jturn += nblk;
     }
   }
 
@@ -414,7 +481,7 @@ int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: cannot reserve %zu bytes of shared memory", smem);
-  const int64_t grid = (int64_t)p.B * p.Hkv * p.ctas_per_kvh;
+  const int grid = std::min(p.n_items, kf::sm_count_current_device());
   kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, p);
   return kf::check_launch("kf_attn_fwd");
 }
@@ -483,6 +550,7 @@ extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   p.m_blocks = (int)((Sq + kBlockM - 1) / kBlockM);
   p.slots_per_kvh = p.G * p.m_blocks;
   p.ctas_per_kvh = (p.slots_per_kvh + 1) / 2;
+  p.n_items = (int)((int64_t)p.B * p.Hkv * p.ctas_per_kvh);
   p.scale_log2 = scale * kLog2e;
   p.status = status;
   if ((int64_t)p.B * p.Hkv * p.ctas_per_kvh > 0x7fffffffLL)

@@ -43,6 +43,8 @@ def test_forward_reference_shapes(head_dim, causal, dtype):
         (1, 2, 2, 130, 77, 20, True),       # head dim not a multiple of 8 (padded)
         (2, 16, 4, 1024, 1024, 128, True),
         (1, 16, 4, 2048, 2048, 96, False),
+        (2, 40, 40, 300, 300, 64, True),   # 160 items > 148 CTAs: persistent CTAs run several,
+        (2, 40, 40, 300, 300, 64, False),  # single-tile items (odd row-block count) among them
     ],
 )
 def test_forward_shapes(b, hq, hkv, sq, sk, d, causal):
