@@ -31,7 +31,6 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kTileKeys = 16;  // keys per warp tile
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -73,7 +72,9 @@ __device__ __forceinline__ uint32_t tma_swz(int r, int c, int rows) {
   return (uint32_t)((c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-constexpr int kTileN = kWarps * kTileKeys;  // 64 keys per TMA tile
+// Keys per K/V tile: 4 warps x 16 keys, or 4 x 32 on the transposed path for
+// head_dim <= 64 (fewer, larger steps per warp).
+__host__ __device__ constexpr int tile_keys(int kw) { return kWarps * kw; }
 
 // NP = 64-column panels of the padded head dim (1 or 2), MT = 16-row m-tiles of
 // packed query rows, STAGES = depth of the K/V ring.
@@ -85,7 +86,7 @@ constexpr int kTileN = kWarps * kTileKeys;  // 64 keys per TMA tile
 // small row counts).  P^T goes from the S^T accumulator layout to the B
 // operand layout with movmatrix (8x8 transposes in registers); the row max
 // and sum reduce across the 8 lane groups that hold a row's keys.
-template <bool BF16, int NP, int MT, int STAGES, bool N8>
+template <bool BF16, int NP, int MT, int STAGES, bool N8, int KW>
 __global__ void __launch_bounds__(kThreads)
 decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                     const DecodeArgs a) {
@@ -93,7 +94,8 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   constexpr int ROWS = N8 ? 8 : MT * 16;
   constexpr int Q_ROW_BYTES = DP * 2;
   constexpr int CHUNKS = DP / 8;                 // 16-byte chunks per row
-  constexpr int PANEL = kTileN * 128;            // one 64-column panel of a tile
+  constexpr int TN = tile_keys(KW);              // keys per K/V tile (KW per warp)
+  constexpr int PANEL = TN * 128;                // one 64-column panel of a tile
   constexpr int TILE = NP * PANEL;               // K (or V) tile bytes
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -109,7 +111,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   const int row0 = blockIdx.z * ROWS;
   const int key_begin = split * a.chunk;
   const int key_end = min(key_begin + a.chunk, a.Sk);
-  const int n_tiles = (key_end - key_begin + kTileN - 1) / kTileN;
+  const int n_tiles = (key_end - key_begin + TN - 1) / TN;
   const bool fused = a.nk != nullptr;
 
   if (tid == 0) {
@@ -138,8 +140,8 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     kf::mbar_arrive_expect_tx(&full[s], 2 * TILE);
 #pragma unroll
     for (int pn = 0; pn < NP; ++pn) {
-      kf::tma_load_4d(kt + pn * PANEL, &map_k, &full[s], pn * 64, key_begin + t * kTileN, kvh, b);
-      kf::tma_load_4d(kt + TILE + pn * PANEL, &map_v, &full[s], pn * 64, key_begin + t * kTileN, kvh, b);
+      kf::tma_load_4d(kt + pn * PANEL, &map_k, &full[s], pn * 64, key_begin + t * TN, kvh, b);
+      kf::tma_load_4d(kt + TILE + pn * PANEL, &map_v, &full[s], pn * 64, key_begin + t * TN, kvh, b);
     }
   };
   if (tid == 0) {
@@ -181,7 +183,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     for (int n = 0; n < DP / 8; ++n) o_acc[mt][n][0] = o_acc[mt][n][1] = o_acc[mt][n][2] = o_acc[mt][n][3] = 0.f;
   }
   const uint32_t sQ_u = kf::smem_u32(sQ);
-  const int wr0 = warp * kTileKeys;   // this warp's 16 rows of every tile
+  const int wr0 = warp * KW;   // this warp's KW rows (keys) of every tile
   // N8 state: Q^T as B fragments (k = head dim, n = row), running max / sum
   // of rows 2 (lane % 4) + {0, 1}, and O^T accumulators (m = head dim).
   uint32_t qb[DP / 16][2];
@@ -224,37 +226,47 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     }
     uint8_t* kt = sKV + st * 2 * TILE;
     uint8_t* vt = kt + TILE;
-    const int key0 = key_begin + t * kTileN + wr0;
-    if (fused && a.past_len >= key0 && a.past_len < key0 + kTileKeys) {
+    const int key0 = key_begin + t * TN + wr0;
+    if (fused && a.past_len >= key0 && a.past_len < key0 + KW) {
       const int r = wr0 + (int)(a.past_len - key0);
       for (int c = lane; c < CHUNKS; c += 32) {
         const bool in = c * 8 < a.D;
         const uint4 kv = in ? *reinterpret_cast<const uint4*>(a.nk + b * a.nks[0] + kvh * a.nks[1] + c * 8) : make_uint4(0, 0, 0, 0);
         const uint4 vv = in ? *reinterpret_cast<const uint4*>(a.nv + b * a.nvs[0] + kvh * a.nvs[1] + c * 8) : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(kt + tma_swz(r, c, kTileN)) = kv;
-        *reinterpret_cast<uint4*>(vt + tma_swz(r, c, kTileN)) = vv;
+        *reinterpret_cast<uint4*>(kt + tma_swz(r, c, TN)) = kv;
+        *reinterpret_cast<uint4*>(vt + tma_swz(r, c, TN)) = vv;
       }
       __syncwarp();
     }
     const uint32_t sk_u = kf::smem_u32(kt), sv_u = kf::smem_u32(vt);
 
     if constexpr (N8) {
-      // S^T (16 keys x 8 rows) = K Q^T
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      // S^T (KW keys x 8 rows) = K Q^T, as KW / 16 independent 16-key halves
+      constexpr int H = KW / 16;
+      float c[H][4];
 #pragma unroll
-      for (int kk = 0; kk < DP / 16; ++kk) {
-        uint32_t ka[4];
-        kf::ldmatrix_x4(ka, sk_u + tma_swz(wr0 + (lane & 15), 2 * kk + (lane >> 4), kTileN));
-        kf::mma_16816<BF16>(c, ka, qb[kk][0], qb[kk][1]);
+      for (int h = 0; h < H; ++h) c[h][0] = c[h][1] = c[h][2] = c[h][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < DP / 16; ++kk)
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          uint32_t ka[4];
+          kf::ldmatrix_x4(ka, sk_u + tma_swz(wr0 + h * 16 + (lane & 15), 2 * kk + (lane >> 4), TN));
+          kf::mma_16816<BF16>(c[h], ka, qb[kk][0], qb[kk][1]);
+        }
+      // rows 2 (lane % 4) + {0, 1}; keys h*16 + lane / 4 (c0, c1) and + 8 (c2, c3)
+      float x[H][4];
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        const int ka0 = key0 + h * 16 + (lane >> 2);
+        x[h][0] = ka0 < key_end ? c[h][0] * a.scale_log2 : -INFINITY;
+        x[h][1] = ka0 < key_end ? c[h][1] * a.scale_log2 : -INFINITY;
+        x[h][2] = ka0 + 8 < key_end ? c[h][2] * a.scale_log2 : -INFINITY;
+        x[h][3] = ka0 + 8 < key_end ? c[h][3] * a.scale_log2 : -INFINITY;
+        mx[0] = kf::fmax3(mx[0], x[h][0], x[h][2]);
+        mx[1] = kf::fmax3(mx[1], x[h][1], x[h][3]);
       }
-      // rows 2 (lane % 4) + {0, 1}; keys lane / 4 (c0, c1) and lane / 4 + 8 (c2, c3)
-      const int ka0 = key0 + (lane >> 2);
-      float x[4];
-      x[0] = ka0 < key_end ? c[0] * a.scale_log2 : -INFINITY;
-      x[1] = ka0 < key_end ? c[1] * a.scale_log2 : -INFINITY;
-      x[2] = ka0 + 8 < key_end ? c[2] * a.scale_log2 : -INFINITY;
-      x[3] = ka0 + 8 < key_end ? c[3] * a.scale_log2 : -INFINITY;
-      float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], off));
@@ -268,10 +280,19 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
         alpha[j] = kf::ex2(m8[j] - mu[j]);
         m8[j] = m_new;
       }
-      const float p0 = kf::ex2(x[0] - mu[0]), p1 = kf::ex2(x[1] - mu[1]);
-      const float p2 = kf::ex2(x[2] - mu[0]), p3 = kf::ex2(x[3] - mu[1]);
-      l8[0] = l8[0] * alpha[0] + (p0 + p2);
-      l8[1] = l8[1] * alpha[1] + (p1 + p3);
+      float pp[H][4];
+      float ls[2] = {0.f, 0.f};
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        pp[h][0] = kf::ex2(x[h][0] - mu[0]);
+        pp[h][1] = kf::ex2(x[h][1] - mu[1]);
+        pp[h][2] = kf::ex2(x[h][2] - mu[0]);
+        pp[h][3] = kf::ex2(x[h][3] - mu[1]);
+        ls[0] += pp[h][0] + pp[h][2];
+        ls[1] += pp[h][1] + pp[h][3];
+      }
+      l8[0] = l8[0] * alpha[0] + ls[0];
+      l8[1] = l8[1] * alpha[1] + ls[1];
       if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
         for (int dm = 0; dm < DP / 16; ++dm) {
@@ -281,16 +302,23 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
           ot[dm][3] *= alpha[1];
         }
       }
-      // P^T as the B operand (k = key, n = row): transpose the two 8x8 halves
-      const uint32_t pb0 = kf::movmatrix_trans(kf::pack2<BF16>(p0, p1));
-      const uint32_t pb1 = kf::movmatrix_trans(kf::pack2<BF16>(p2, p3));
+      // P^T as the B operand (k = key, n = row): transpose the 8x8 blocks
+      uint32_t pb[H][2];
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        pb[h][0] = kf::movmatrix_trans(kf::pack2<BF16>(pp[h][0], pp[h][1]));
+        pb[h][1] = kf::movmatrix_trans(kf::pack2<BF16>(pp[h][2], pp[h][3]));
+      }
       // O^T (head dim x 8 rows) += V^T P^T
 #pragma unroll
-      for (int dm = 0; dm < DP / 16; ++dm) {
-        uint32_t va[4];
-        kf::ldmatrix_x4_trans(va, sv_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * dm + ((lane >> 3) & 1), kTileN));
-        kf::mma_16816<BF16>(ot[dm], va, pb0, pb1);
-      }
+      for (int dm = 0; dm < DP / 16; ++dm)
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          uint32_t va[4];
+          kf::ldmatrix_x4_trans(va, sv_u + tma_swz(wr0 + h * 16 + (lane & 7) + ((lane >> 4) << 3),
+                                                   2 * dm + ((lane >> 3) & 1), TN));
+          kf::mma_16816<BF16>(ot[dm], va, pb[h][0], pb[h][1]);
+        }
     } else {
       // S = Q K^T for this warp's 16 keys
       float sc[MT][2][4];
@@ -301,7 +329,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   #pragma unroll
       for (int kk = 0; kk < DP / 16; ++kk) {
         uint32_t kb[4];
-        kf::ldmatrix_x4(kb, sk_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), kTileN));
+        kf::ldmatrix_x4(kb, sk_u + tma_swz(wr0 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1), TN));
   #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           uint32_t qa[4];
@@ -347,7 +375,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   #pragma unroll
         for (int dn = 0; dn < DP / 16; ++dn) {
           uint32_t vb[4];
-          kf::ldmatrix_x4_trans(vb, sv_u + tma_swz(wr0 + (lane & 15), 2 * dn + (lane >> 4), kTileN));
+          kf::ldmatrix_x4_trans(vb, sv_u + tma_swz(wr0 + (lane & 15), 2 * dn + (lane >> 4), TN));
           kf::mma_16816<BF16>(o_acc[mt][2 * dn], pa, vb[0], vb[1]);
           kf::mma_16816<BF16>(o_acc[mt][2 * dn + 1], pa, vb[2], vb[3]);
         }
@@ -631,6 +659,10 @@ int launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
   return kf::check_launch(what);
 }
 
+// Keys per K/V tile of the kernel variant dispatch_split picks; split chunks
+// are multiples of it.
+int decode_tile_keys(int64_t rows, int64_t D) { return (rows <= 8 && D <= 64) ? tile_keys(32) : tile_keys(16); }
+
 template <bool BF16>
 int launch_merge(const MergeArgs& m, cudaStream_t st) {
   const int groups = kMergeThreads / (m.D / 4);
@@ -642,16 +674,16 @@ int launch_merge(const MergeArgs& m, cudaStream_t st) {
   return launch_dependent(merge_kernel<BF16>, dim3((unsigned)m.rows), dim3(kMergeThreads), smem, st, "kf merge", m);
 }
 
-template <bool BF16, int NP, int MT, bool N8 = false>
+template <bool BF16, int NP, int MT, bool N8 = false, int KW = 16>
 int launch_split(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, int row_blocks,
                  cudaStream_t st) {
-  constexpr int STAGES = NP == 1 ? 4 : 2;
+  constexpr int STAGES = KW == 32 ? 3 : (NP == 1 ? 4 : 2);
   constexpr int DP = NP * 64;
   constexpr int ROWS = N8 ? 8 : MT * 16;
-  const size_t pipe = 1024 + (size_t)STAGES * 2 * NP * kTileN * 128 + (size_t)ROWS * DP * 2;
+  const size_t pipe = 1024 + (size_t)STAGES * 2 * NP * tile_keys(KW) * 128 + (size_t)ROWS * DP * 2;
   const size_t merge = 1024 + (size_t)kWarps * ROWS * 3 * 4 + ROWS * 4 + (size_t)kWarps * ROWS * DP * 4;
   const size_t smem = pipe > merge ? pipe : merge;
-  auto kern = decode_split_kernel<BF16, NP, MT, STAGES, N8>;
+  auto kern = decode_split_kernel<BF16, NP, MT, STAGES, N8, KW>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
   dim3 grid(a.num_splits, a.B * a.Hkv, row_blocks);
@@ -662,12 +694,13 @@ template <bool BF16>
 int dispatch_split(const DecodeArgs& a, const kf_tensor4* k, const kf_tensor4* v, cudaStream_t st) {
   CUtensorMap mk, mv;
   int rc;
-  if ((rc = kf::encode_tmap_4d(&mk, k, 64, kTileN))) return rc;
-  if ((rc = kf::encode_tmap_4d(&mv, v, 64, kTileN))) return rc;
   const int np = a.D <= 64 ? 1 : 2;
+  const int tn = decode_tile_keys(a.rows, a.D);
+  if ((rc = kf::encode_tmap_4d(&mk, k, 64, tn))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mv, v, 64, tn))) return rc;
   if (a.rows <= 8)  // transposed products: rows on the n = 8 side
-    return np == 1 ? launch_split<BF16, 1, 1, true>(a, mk, mv, 1, st)
-                   : launch_split<BF16, 2, 1, true>(a, mk, mv, 1, st);
+    return np == 1 ? launch_split<BF16, 1, 1, true, 32>(a, mk, mv, 1, st)
+                   : launch_split<BF16, 2, 1, true, 16>(a, mk, mv, 1, st);
   const int mt_max = np == 1 ? 4 : 2;
   int mt = (a.rows + 15) / 16;
   if (mt > mt_max) mt = mt_max;
@@ -761,7 +794,8 @@ extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tens
   if (num_splits <= 0)
     num_splits = kf_decode_num_splits(B, Hq, Hkv, Sq, Sk, D, kf::sm_count_current_device());
   if (num_splits > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many splits");
-  const int64_t chunk = cdiv64(cdiv64(Sk, num_splits), 64) * 64;
+  const int64_t tk = decode_tile_keys(Hq / Hkv * Sq, D);
+  const int64_t chunk = cdiv64(cdiv64(Sk, num_splits), tk) * tk;
   num_splits = (int)cdiv64(Sk, chunk);
 
   DecodeArgs a;
