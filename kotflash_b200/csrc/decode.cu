@@ -510,6 +510,299 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
   }
 }
 
+// K3 on the tensor cores, for more than 16 packed rows (e.g. 4-way GQA with
+// Sq >= 5) and no fused append: with several 16-row m tiles the warp-MMA
+// version is bound by its MMAs, which tcgen05 takes off the critical path
+// (one M = 128 tile covers up to 128 rows).
+// CTA = (split, batch, KV head, block of up to 128 packed rows); rows sit on
+// TMEM lanes (M = 128, unused lanes are zero rows whose warps skip the
+// softmax).  Per 128-key tile: S = Q K^T (SS), softmax by one thread per row
+// (lazy rescale, P written back over S as 16-bit), O += P V (TS).  Warps 0-3
+// softmax + Q load, warp 4 TMEM allocation + MMA issue, warp 5 TMA producer.
+constexpr int kTcThreads = 192;
+constexpr int kTcKeys = 128;
+constexpr int kTcStages = 2;
+constexpr float kTcRescale = 8.0f;  // log2 units, as in the prefill forward
+
+struct __align__(8) TcBarriers {
+  uint64_t full[kTcStages], empty[kTcStages];
+  uint64_t q_ready, s_full, p_full, o_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcBarriers* bars, int32_t* status) {
+  if (kf::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = kf::global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (kf::mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    if ((++spins & 15u) == 0) {
+      if (*(volatile int*)&bars->abort_flag) return false;
+      if (kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
+        *(volatile int*)&bars->abort_flag = 1;
+        if (status) atomicExch(status, KF_DEV_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+template <bool BF16, int NP, int KS>
+__global__ void __launch_bounds__(kTcThreads, 2)
+decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                 const DecodeArgs a) {
+  constexpr int PANEL = kTcKeys * 128;   // 64 columns x 128 rows, 128-byte swizzle
+  constexpr int TILE = NP * PANEL;
+  constexpr int d_pad16 = KS * 16;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sK = smem;                          // [stage][NP][128 keys][64]
+  uint8_t* sV = sK + kTcStages * TILE;
+  uint8_t* sQ = sV + kTcStages * TILE;         // [NP][128 rows][64]
+  TcBarriers* bars = reinterpret_cast<TcBarriers*>(sQ + TILE);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x;
+  const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  const int row0 = blockIdx.z * 128;
+  const int valid_rows = min(128, a.rows - row0);
+  const int active_warps = (valid_rows + 31) / 32;   // softmax warps holding real rows
+  const int key_begin = split * a.chunk;
+  const int key_end = min(key_begin + a.chunk, a.Sk);
+  const int n_tiles = (key_end - key_begin + kTcKeys - 1) / kTcKeys;
+
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      kf::mbar_init(&bars->full[s], 1);
+      kf::mbar_init(&bars->empty[s], 1);
+    }
+    kf::mbar_init(&bars->q_ready, 128);
+    kf::mbar_init(&bars->s_full, 1);
+    kf::mbar_init(&bars->p_full, 32 * active_warps);
+    kf::mbar_init(&bars->o_done, 1);
+    bars->abort_flag = 0;
+    kf::fence_barrier_init();
+  }
+  if (warp == 4) {
+    kf::tmem_alloc(&bars->tmem_base, 256);
+    kf::tmem_relinquish();
+  }
+  if (warp == 5 && lane == 0) {
+    kf::tma_prefetch_desc(&map_k);
+    kf::tma_prefetch_desc(&map_v);
+  }
+  kf::tc_fence_before();
+  __syncthreads();
+  kf::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  // programmatic dependent launch: see decode_split_kernel
+  kf::griddep_wait();
+  kf::griddep_launch_dependents();
+
+  if (warp == 5) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t % kTcStages;
+        if (!tc_wait(&bars->empty[s], ((t / kTcStages) & 1) ^ 1, bars, a.status)) break;
+        ++issued;
+        kf::mbar_arrive_expect_tx(&bars->full[s], 2 * TILE);
+        for (int pn = 0; pn < NP; ++pn) {
+          kf::tma_load_4d(sK + s * TILE + pn * PANEL, &map_k, &bars->full[s], pn * 64,
+                          key_begin + t * kTcKeys, kvh, b);
+          kf::tma_load_4d(sV + s * TILE + pn * PANEL, &map_v, &bars->full[s], pn * 64,
+                          key_begin + t * kTcKeys, kvh, b);
+        }
+      }
+      if (*(volatile int*)&bars->abort_flag) {
+        // let loads still in flight land (bounded) before the CTA exits
+        for (int t2 = max(0, issued - kTcStages); t2 < issued; ++t2)
+          kf::mbar_wait(&bars->full[t2 % kTcStages], (t2 / kTcStages) & 1, nullptr, 100000000ull);
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = kf::make_idesc_f16(BF16, 128, kTcKeys, 0, 0);
+      const uint32_t idesc_pv = kf::make_idesc_f16(BF16, 128, d_pad16, 0, 1);
+      const kf::SDesc dq = kf::make_sdesc_split(kf::smem_u32(sQ), 16, 1024);
+      const kf::SDesc dk = kf::make_sdesc_split(kf::smem_u32(sK), 16, 1024);
+      const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), PANEL, 1024);
+      bool ok = tc_wait(&bars->q_ready, 0, bars, a.status);
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int s = t % kTcStages;
+        if (!(ok = tc_wait(&bars->full[s], (t / kTcStages) & 1, bars, a.status))) break;
+        kf::tc_fence_after();
+        const uint32_t koff = s * TILE;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
+          kf::umma_ss(tmem, kf::sdesc_at(dq, off), kf::sdesc_at(dk, koff + off), idesc_qk, kk > 0);
+        }
+        kf::umma_commit(&bars->s_full);
+        if (!(ok = tc_wait(&bars->p_full, t & 1, bars, a.status))) break;
+        kf::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTcKeys / 16; ++kk)
+          kf::umma_ts(tmem + 128, tmem + kk * 8, kf::sdesc_at(dv, koff + kk * 2048), idesc_pv,
+                      (t > 0 || kk > 0));
+        kf::umma_commit(&bars->empty[s]);
+      }
+      kf::umma_commit(&bars->o_done);
+    }
+  } else {
+    // ------------------------------------------------------------ Q load + softmax (thread = row)
+    constexpr int CH = NP * 8;  // 16-byte chunks per row
+    {
+      const int r = tid;        // tile row == TMEM lane
+      const int pr = row0 + r;
+      const bool in = r < valid_rows;
+      const int g = in ? pr / a.Sq : 0, sq = in ? pr % a.Sq : 0;
+      const uint16_t* src = a.q + b * a.qs[0] + (int64_t)(kvh * a.G + g) * a.qs[1] + sq * a.qs[2];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const bool ok = in && c * 8 < a.D;
+        kf::cp_async16(sQ + (c >> 3) * PANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4), src + (ok ? c * 8 : 0), ok);
+      }
+      kf::cp_async_commit();
+      kf::cp_async_wait<0>();
+      kf::fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+      kf::mbar_arrive(&bars->q_ready);
+    }
+    const int r = tid;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    float m_ref = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    if (warp < active_warps) {
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        if (!(ok = tc_wait(&bars->s_full, t & 1, bars, a.status))) break;
+        kf::tc_fence_after();
+        uint32_t sr[128];
+        kf::tmem_ld32(lane_base + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        kf::tmem_ld32(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        kf::tmem_ld32(lane_base + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+        kf::tmem_ld32(lane_base + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        kf::tmem_wait_ld();
+        const int key0 = key_begin + t * kTcKeys;
+        const int lim = key_end - key0;  // keys past the split's end are masked
+        if (lim < kTcKeys) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c >= lim) sr[c] = 0xFF800000u;
+        }
+        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; c += 8) {
+          a0 = kf::fmax3(a0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
+          a1 = kf::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          a2 = kf::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          a3 = kf::fmax3(a3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+        }
+        const float mx = kf::fmax3(a0, a1, fmaxf(a2, a3)) * a.scale_log2;
+        float alpha = 1.f;
+        bool rescale_o = false;
+        if (t == 0) {
+          m_ref = mx;
+        } else if (mx > m_ref + kTcRescale) {
+          alpha = kf::ex2(m_ref - mx);
+          m_ref = mx;
+          rescale_o = true;
+        }
+        const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+        l_sum *= alpha;
+        uint32_t pk[64];
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float p0 = kf::ex2(__uint_as_float(sr[2 * c]) * a.scale_log2 - m_use);
+          const float p1 = kf::ex2(__uint_as_float(sr[2 * c + 1]) * a.scale_log2 - m_use);
+          sum += p0 + p1;
+          pk[c] = kf::pack2<BF16>(p0, p1);
+        }
+        l_sum += sum;
+        kf::tmem_st32(lane_base + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+        kf::tmem_st32(lane_base + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          // O row *= alpha; the S commit of this tile covers the previous PV
+          for (int c0 = 0; c0 < d_pad16; c0 += 16) {
+            uint32_t orow[16];
+            kf::tmem_ld16(lane_base + 128 + c0, orow);
+            kf::tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+            kf::tmem_st16(lane_base + 128 + c0, orow);
+          }
+        }
+        kf::tmem_wait_st();
+        kf::tc_fence_before();
+        kf::mbar_arrive(&bars->p_full);
+      }
+      // ---------------------------------------------------------- epilogue
+      if (ok && tc_wait(&bars->o_done, 0, bars, a.status)) {
+        kf::tc_fence_after();
+        const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        const float row_lse = l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;
+        const bool row_ok = r < valid_rows;
+        const int pr = row0 + r;
+        const int64_t prow = (int64_t)(b * a.Hkv + kvh) * a.rows + pr;
+        for (int c0 = 0; c0 < d_pad16; c0 += 16) {
+          uint32_t ov[16];
+          kf::tmem_ld16(lane_base + 128 + c0, ov);
+          kf::tmem_wait_ld();
+          if (!row_ok) continue;
+          if (a.num_splits == 1) {
+            uint16_t* dst = a.o + b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2];
+#pragma unroll
+            for (int c = 0; c < 16; c += 2)
+              if (c0 + c < a.D)
+                *reinterpret_cast<uint32_t*>(dst + c0 + c) =
+                    kf::pack2<BF16>(__uint_as_float(ov[c]) * inv_l, __uint_as_float(ov[c + 1]) * inv_l);
+          } else {
+            float* dst = a.part_o + ((int64_t)split * a.prow_total + prow) * a.D;
+#pragma unroll
+            for (int c = 0; c < 16; c += 4)
+              if (c0 + c < a.D)
+                *reinterpret_cast<float4*>(dst + c0 + c) =
+                    make_float4(__uint_as_float(ov[c]) * inv_l, __uint_as_float(ov[c + 1]) * inv_l,
+                                __uint_as_float(ov[c + 2]) * inv_l, __uint_as_float(ov[c + 3]) * inv_l);
+          }
+        }
+        if (row_ok) {
+          if (a.num_splits == 1) {
+            if (a.lse) a.lse[prow] = row_lse;
+          } else {
+            a.part_lse[(int64_t)split * a.prow_total + prow] = row_lse;
+          }
+        }
+      }
+    }
+    if (!ok) {
+      // a bounded wait expired: NaN outputs instead of stale data
+      const int pr = row0 + r;
+      if (r < valid_rows) {
+        const int64_t prow = (int64_t)(b * a.Hkv + kvh) * a.rows + pr;
+        for (int c = 0; c < a.D; ++c) {
+          if (a.num_splits == 1)
+            a.o[b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2] + c] = 0x7fffu;
+          else
+            a.part_o[((int64_t)split * a.prow_total + prow) * a.D + c] = __int_as_float(0x7fc00000);
+        }
+        if (a.num_splits > 1) a.part_lse[(int64_t)split * a.prow_total + prow] = 0.f;
+      }
+    }
+  }
+
+  kf::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    kf::tc_fence_after();
+    kf::tmem_dealloc(tmem, 256);
+  }
+}
+
 // K3b: merge of S split partials by their LSE weights.
 struct MergeArgs {
   const float* part_o;
@@ -661,7 +954,10 @@ int launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 // Keys per K/V tile of the kernel variant dispatch_split picks; split chunks
 // are multiples of it.
-int decode_tile_keys(int64_t rows, int64_t D) { return (rows <= 8 && D <= 64) ? tile_keys(32) : tile_keys(16); }
+int decode_tile_keys(int64_t rows, int64_t D, bool fused) {
+  if (rows > 16 && !fused) return kTcKeys;
+  return (rows <= 8 && D <= 64) ? tile_keys(32) : tile_keys(16);
+}
 
 template <bool BF16>
 int launch_merge(const MergeArgs& m, cudaStream_t st) {
@@ -690,12 +986,43 @@ int launch_split(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& 
   return launch_dependent(kern, grid, dim3(kThreads), smem, st, "kf_decode", mk, mv, a);
 }
 
+template <bool BF16, int KS>
+int launch_tc(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
+  constexpr int NP = KS > 4 ? 2 : 1;
+  constexpr size_t TILE = (size_t)NP * kTcKeys * 128;
+  const size_t smem = 1024 + (2 * kTcStages + 1) * TILE + sizeof(TcBarriers);
+  auto kern = decode_tc_kernel<BF16, NP, KS>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
+  dim3 grid(a.num_splits, a.B * a.Hkv, (a.rows + 127) / 128);
+  return launch_dependent(kern, grid, dim3(kTcThreads), smem, st, "kf_decode", mk, mv, a);
+}
+
+template <bool BF16>
+int dispatch_tc(const DecodeArgs& a, const kf_tensor4* k, const kf_tensor4* v, cudaStream_t st) {
+  CUtensorMap mk, mv;
+  int rc;
+  if ((rc = kf::encode_tmap_4d(&mk, k, 64, kTcKeys))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mv, v, 64, kTcKeys))) return rc;
+  switch ((a.D + 15) / 16) {
+    case 1: return launch_tc<BF16, 1>(a, mk, mv, st);
+    case 2: return launch_tc<BF16, 2>(a, mk, mv, st);
+    case 3: return launch_tc<BF16, 3>(a, mk, mv, st);
+    case 4: return launch_tc<BF16, 4>(a, mk, mv, st);
+    case 5: return launch_tc<BF16, 5>(a, mk, mv, st);
+    case 6: return launch_tc<BF16, 6>(a, mk, mv, st);
+    case 7: return launch_tc<BF16, 7>(a, mk, mv, st);
+    default: return launch_tc<BF16, 8>(a, mk, mv, st);
+  }
+}
+
 template <bool BF16>
 int dispatch_split(const DecodeArgs& a, const kf_tensor4* k, const kf_tensor4* v, cudaStream_t st) {
+  if (a.rows > 16 && a.nk == nullptr) return dispatch_tc<BF16>(a, k, v, st);
   CUtensorMap mk, mv;
   int rc;
   const int np = a.D <= 64 ? 1 : 2;
-  const int tn = decode_tile_keys(a.rows, a.D);
+  const int tn = decode_tile_keys(a.rows, a.D, a.nk != nullptr);
   if ((rc = kf::encode_tmap_4d(&mk, k, 64, tn))) return rc;
   if ((rc = kf::encode_tmap_4d(&mv, v, 64, tn))) return rc;
   if (a.rows <= 8)  // transposed products: rows on the n = 8 side
@@ -794,7 +1121,7 @@ extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tens
   if (num_splits <= 0)
     num_splits = kf_decode_num_splits(B, Hq, Hkv, Sq, Sk, D, kf::sm_count_current_device());
   if (num_splits > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many splits");
-  const int64_t tk = decode_tile_keys(Hq / Hkv * Sq, D);
+  const int64_t tk = decode_tile_keys(Hq / Hkv * Sq, D, fused);
   const int64_t chunk = cdiv64(cdiv64(Sk, num_splits), tk) * tk;
   num_splits = (int)cdiv64(Sk, chunk);
 

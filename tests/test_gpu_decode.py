@@ -68,6 +68,20 @@ def test_decode_head_dims_and_dtypes(dtype, d):
     check_close(out, exp, name=f"decode D{d} {dtype}")
 
 
+
+@pytest.mark.parametrize("hq,hkv,sq,d,sk", [(8, 2, 5, 96, 3000), (8, 2, 16, 128, 1500), (4, 1, 5, 72, 777),
+                                            (32, 2, 16, 64, 2049), (16, 1, 9, 16, 300)])
+def test_decode_tensor_core_path(hq, hkv, sq, d, sk):
+    """More than 16 packed rows per KV head (tcgen05 decode), incl. head dims that
+    pad to two 64-column panels and more than 128 rows (two row blocks)."""
+    q = _rand((2, hq, sq, d), torch.bfloat16, 41)
+    k = _rand((2, hkv, sk, d), torch.bfloat16, 42)
+    v = _rand((2, hkv, sk, d), torch.bfloat16, 43)
+    out, lse = _decode_forward(q, k, v, scale=d ** -0.5, want_lse=True)
+    exp_o, exp_lse = oracle.forward(q, k, v, causal=False, scale=d ** -0.5)
+    check_close(out, exp_o, name=f"tc decode O {hq},{hkv},{sq},{d},{sk}")
+    check_close(lse, exp_lse, name=f"tc decode LSE {hq},{hkv},{sq},{d},{sk}")
+
 def test_strided_cache_decode_reads_prefix_in_place():
     # reference tests/test_triton.py:212-240 at the BASELINE cfg4 geometry
     torch.manual_seed(29)
