@@ -445,10 +445,12 @@ def bench_odd_head_dim(peaks):
 def bench_decode_multi_gpu(world, rank):
     """cfg3 at Sk=131072 with the KV sequence split across ranks.
 
-    Each rank's sequence (split-KV decode of its chunk, pack, NCCL all-gather,
-    LSE merge) is captured in a CUDA graph and replayed; the compute-only part
-    is captured separately so compute and exchange are reported apart.  Max
-    over ranks of device time per call."""
+    Each rank's sequence (split-KV decode of its chunk, then the exchange of
+    partials and the LSE merge) is captured in a CUDA graph and replayed; the
+    compute-only part is captured separately so compute and exchange are
+    reported apart.  Two exchanges: NVLink peer memory (``PeerExchange``, two
+    kernels) and the NCCL route (pack, all-gather, merge).  Max over ranks of
+    device time per call."""
     from kotflash_b200 import distributed as kd
     from kotflash_b200.attention import _decode_forward
 
@@ -462,22 +464,35 @@ def bench_decode_multi_gpu(world, rank):
         q = torch.randn(2, 8, sq, 64, device="cuda", generator=g).half()
         kl, vl = k_full[:, :, lo:hi].contiguous(), v_full[:, :, lo:hi].contiguous()
         del k_full, v_full
+        ex = kd.PeerExchange(rows=q[..., 0].numel(), d=64, dtype=q.dtype)
 
-        def full(_i):
+        def nccl(_i):
             kd.decode_kv_split(q, kl, vl, scale=0.125)
+
+        def peer(_i):
+            kd.decode_kv_split(q, kl, vl, scale=0.125, exchange=ex)
 
         def local(_i):
             _decode_forward(q, kl, vl, scale=0.125, want_lse=True)
 
         barrier(world)
-        t_all = _graph_time(full, 8, replays=5)
+        t_n = _graph_time(nccl, 8, replays=5)
+        barrier(world)
+        t_p = _graph_time(peer, 32, replays=5)
         barrier(world)
         t_c = _graph_time(local, 8, replays=5)
-        a = max_over_ranks(t_all, world)
+        n = max_over_ranks(t_n, world)
+        pp = max_over_ranks(t_p, world)
         c = max_over_ranks(t_c, world)
+        timeouts = max_over_ranks(float(ex.status()), world)
+        barrier(world)
+        ex.close()
         out.append({"sq": sq, "sk": sk, "ranks": world, "keys_per_rank": hi - lo,
-                    "compute_us": round(c * 1e3, 2), "exchange_merge_us": round((a - c) * 1e3, 2),
-                    "total_us": round(a * 1e3, 2), "us_per_token": round(a * 1e3 / sq, 3),
+                    "compute_us": round(c * 1e3, 2),
+                    "peer": {"exchange_merge_us": round((pp - c) * 1e3, 2), "total_us": round(pp * 1e3, 2),
+                             "us_per_token": round(pp * 1e3 / sq, 3), "timeouts": int(timeouts)},
+                    "nccl": {"exchange_merge_us": round((n - c) * 1e3, 2), "total_us": round(n * 1e3, 2),
+                             "us_per_token": round(n * 1e3 / sq, 3)},
                     "timing": "CUDA-graph replay, max over ranks"})
         torch.cuda.synchronize()
     return out

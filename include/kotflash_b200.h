@@ -145,6 +145,46 @@ int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits
                       int64_t rows, int64_t D, void* o, float* lse, int dtype,
                       void* stream);
 
+/* ---- cross-GPU exchange of decode partials over NVLink peer memory -----
+ * No counterpart in the reference, which has no multi-GPU decode; it
+ * replaces the all-gather + merge of a KV-sequence split across the ranks of
+ * one box (the split/merge math is triton_forward.py:270-349 applied across
+ * ranks).  Each rank owns a mailbox of kf_peer_mailbox_bytes(world, rows, D)
+ * bytes of ZERO-FILLED device memory from cudaMalloc (256-byte aligned) and
+ * maps every peer's through CUDA IPC: kf_ipc_get_handle gives a 64-byte
+ * handle plus the pointer's offset inside its allocation, kf_ipc_open_handle
+ * maps a peer's handle in this process, kf_ipc_close_handle unmaps it.
+ *
+ * kf_decode_peer_exchange: o [rows, D] (fp16/bf16, this rank's normalised
+ * partial output, contiguous) and lse [rows] fp32 (natural log) are sent to
+ * every rank with plain peer stores and a system-scope release flag; the
+ * second kernel waits until all `world` partials of this call have arrived
+ * in this rank's mailbox (bounded: about one second, then *status =
+ * KF_DEV_TIMEOUT and out = NaN) and writes the LSE merge into out [rows, D]
+ * and out_lse [rows] (may be null).  mailboxes[r] is rank r's mailbox as
+ * mapped here (mailboxes[rank] is the local one).  Every rank must make the
+ * same sequence of calls with the same rows and D (the call count is kept
+ * in the mailbox, so the two launches may be captured in a CUDA graph and
+ * replayed).  1 <= world <= 8; D a multiple of 8 in [8, 128].  After a
+ * timeout the mailboxes must be zeroed on every rank before the next call.
+ *
+ * kf_decode_peer_put / kf_decode_peer_merge are its two halves.  The put
+ * never waits; the merge waits for the flags of all `world` puts of the
+ * current call, so a single process may drive several mailboxes on one GPU
+ * (all puts first, then the merges) without kernels that wait on one
+ * another. */
+size_t kf_peer_mailbox_bytes(int world, int64_t rows, int64_t D);
+int kf_ipc_get_handle(const void* ptr, void* handle64, uint64_t* offset);
+int kf_ipc_open_handle(const void* handle64, uint64_t offset, void** ptr);
+int kf_ipc_close_handle(void* ptr, uint64_t offset);
+int kf_decode_peer_exchange(const void* o, const float* lse, int64_t rows, int64_t D,
+                            int dtype, void* const* mailboxes, int world, int rank,
+                            void* out, float* out_lse, int32_t* status, void* stream);
+int kf_decode_peer_put(const void* o, const float* lse, int64_t rows, int64_t D, int dtype,
+                       void* const* mailboxes, int world, int rank, void* stream);
+int kf_decode_peer_merge(void* mailbox, int64_t rows, int64_t D, int dtype, int world,
+                         void* out, float* out_lse, int32_t* status, void* stream);
+
 /* ---- self-test of the bounded device wait -------------------------------
  * No counterpart in the reference.  Launches one kernel that waits on a
  * barrier nothing completes; after `budget_us` microseconds the wait gives

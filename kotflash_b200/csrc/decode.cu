@@ -22,6 +22,9 @@
 //    (O normalised, LSE natural log) that the merge kernel combines.
 #include <math.h>
 
+#include <string.h>
+
+#include <mutex>
 #include <utility>
 
 #include "kf_host.h"
@@ -826,19 +829,17 @@ constexpr int kMergeThreads = 256;
 constexpr int kMergeBatch = 8;  // partial loads in flight per thread
 
 template <bool BF16>
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeArgs a) {
+__device__ __forceinline__ void merge_row(const MergeArgs& a, const int64_t row) {
   extern __shared__ float sm[];          // [S] weights, then [G][D] partial sums
   float* wts = sm;
   float* part = sm + ((a.S + 3) & ~3);
   __shared__ float red[kMergeThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t row = blockIdx.x;
   const int tpr = a.D / 4;               // threads per split (one 4-column chunk each)
   const int groups = kMergeThreads / tpr;
   const int c = tid % tpr, g = tid / tpr;
   const float* src = a.part_o + row * a.D + c * 4;
   const int64_t sstride = a.rows * a.D;
-  kf::griddep_wait();  // partials of the split kernel (launched as its programmatic dependent)
 
   float4 pb[kMergeBatch];
 #pragma unroll
@@ -926,6 +927,12 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeArgs a)
     *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
     if (tid == 0 && a.lse) a.lse[row] = den > 0.f ? mx + logf(den) : -INFINITY;
   }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const MergeArgs a) {
+  kf::griddep_wait();  // partials of the split kernel (launched as its programmatic dependent)
+  merge_row<BF16>(a, blockIdx.x);
 }
 
 // Launch with programmatic stream serialization: the kernel may be scheduled
@@ -1238,7 +1245,6 @@ extern "C" int kf_merge_partials(const float* part_o, const float* part_lse, int
 // rows before the merge reads them), but calls that overlap on the GPU (two
 // streams, or two threads' streams) race on the array: serialise them.
 // ---------------------------------------------------------------------------
-#include <mutex>
 
 namespace {
 constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
@@ -1302,4 +1308,293 @@ extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const
   }
   return kf_decode(q, k, v, new_k, new_v, past_len, o, lse, dtype, scale, (int)splits, scratch,
                    splits > 1 ? kNoAllocScratchBytes : 0, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Cross-GPU exchange of decode partials through NVLink peer memory.
+//
+// Long-context decode splits the KV sequence over the ranks of one box; each
+// rank ends with a partial (O, LSE) of its chunk, and every rank needs the
+// merge of all of them.  Instead of a library all-gather followed by a merge
+// launch, each rank owns a mailbox in its own memory that every peer can
+// write (CUDA IPC mapping, peer access over NVLink/NVSwitch; no multicast):
+//   put:   CTA p stores this rank's partial (converted to fp32) into slot
+//          [rank] of rank p's mailbox with plain peer stores, then publishes
+//          it with a system-scope release store of the epoch into a flag;
+//   merge: every CTA waits (bounded) until all W flags of its own mailbox
+//          show the epoch, then merges the W partials (the split-merge math).
+// The epoch lives in the mailbox (advanced by the last merge CTA), so the
+// exchange works unchanged inside CUDA graphs; mailbox halves alternate by
+// epoch parity, and a rank cannot reach epoch e + 2 before every peer has
+// finished merging epoch e (its merge of e + 1 needs their put of e + 1,
+// which follows their merge of e in stream order).
+//
+namespace {
+
+// Mailbox layout: [0, 256) control words {completed epochs, done ticket},
+// then two halves of {O [W][rows][D] fp32, LSE [W][rows] fp32,
+// flags [W][kPeerChunks]}.  Each sender's partial travels in up to
+// kPeerChunks pieces, one CTA and one flag each.
+constexpr int kMaxPeers = 8;
+constexpr int kPeerChunks = 16;
+constexpr int kPeerThreads = 256;
+
+struct PeerLayout {
+  int64_t o_bytes, lse_bytes, flag_bytes, half;
+  int chunks;  // pieces per sender: same on every rank (depends on rows and D only)
+};
+
+__host__ __device__ inline PeerLayout peer_layout(int world, int64_t rows, int D) {
+  PeerLayout L;
+  L.o_bytes = ((int64_t)world * rows * D * 4 + 255) & ~int64_t(255);
+  L.lse_bytes = ((int64_t)world * rows * 4 + 255) & ~int64_t(255);
+  L.flag_bytes = ((int64_t)world * kPeerChunks * 4 + 255) & ~int64_t(255);
+  L.half = L.o_bytes + L.lse_bytes + L.flag_bytes;
+  const int64_t pieces = (rows * D * 4 + 16383) / 16384;  // ~16 KB of fp32 O per CTA
+  L.chunks = (int)(pieces < 1 ? 1 : (pieces > kPeerChunks ? kPeerChunks : pieces));
+  return L;
+}
+
+struct PeerSet {
+  uint8_t* mailbox[kMaxPeers];  // every rank's mailbox base, this rank's own included
+};
+
+KF_DEVI void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+KF_DEVI uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// grid (chunks, world): CTA (c, p) sends piece c of this rank's partial to rank p.
+template <bool BF16>
+__global__ void __launch_bounds__(kPeerThreads) peer_put_kernel(const uint16_t* o, const float* lse, int64_t rows,
+                                                                int D, const __grid_constant__ PeerSet peers,
+                                                                int world, int rank) {
+  kf::griddep_launch_dependents();  // the merge may launch now; it waits for the flags, not for this grid
+  const PeerLayout L = peer_layout(world, rows, D);
+  const uint32_t* ctrl = reinterpret_cast<const uint32_t*>(peers.mailbox[rank]);
+  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(ctrl) + 1;
+  uint8_t* half = peers.mailbox[blockIdx.y] + 256 + (e & 1) * L.half;
+  float* dst_o = reinterpret_cast<float*>(half) + (int64_t)rank * rows * D;
+  float* dst_lse = reinterpret_cast<float*>(half + L.o_bytes) + (int64_t)rank * rows;
+  uint32_t* flag = reinterpret_cast<uint32_t*>(half + L.o_bytes + L.lse_bytes) + rank * kPeerChunks + blockIdx.x;
+  const int64_t n8 = rows * D / 8;  // D % 8 == 0
+  const int64_t per = (n8 + L.chunks - 1) / L.chunks;
+  const int64_t i0 = blockIdx.x * per, i1 = i0 + per < n8 ? i0 + per : n8;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const uint4 v = reinterpret_cast<const uint4*>(o)[i];
+    const float2 f0 = kf::unpack2<BF16>(v.x), f1 = kf::unpack2<BF16>(v.y);
+    const float2 f2 = kf::unpack2<BF16>(v.z), f3 = kf::unpack2<BF16>(v.w);
+    reinterpret_cast<float4*>(dst_o)[2 * i] = make_float4(f0.x, f0.y, f1.x, f1.y);
+    reinterpret_cast<float4*>(dst_o)[2 * i + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) dst_lse[i] = lse[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(flag, e);
+  }
+}
+
+// grid rows: waits (bounded) for every sender's pieces of this epoch, merges
+// one row, and the last CTA advances the epoch.
+template <bool BF16>
+__global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(MergeArgs m, uint8_t* mailbox,
+                                                                    int world, int32_t* status) {
+  static_assert(kMergeThreads >= kMaxPeers * kPeerChunks, "one flag per thread");
+  __shared__ uint32_t s_e;
+  const PeerLayout L = peer_layout(world, m.rows, m.D);
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(mailbox);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctrl) + 1;
+  const uint8_t* half = mailbox + 256 + (e & 1) * L.half;
+  int ok = 1;
+  if (threadIdx.x < world * kPeerChunks && (int)(threadIdx.x % kPeerChunks) < L.chunks) {
+    const uint32_t* flag = reinterpret_cast<const uint32_t*>(half + L.o_bytes + L.lse_bytes) + threadIdx.x;
+    const uint64_t t0 = kf::global_timer_ns();
+    uint32_t spins = 0;
+    while (ld_acquire_sys(flag) != e) {
+      __nanosleep(32);
+      if ((++spins & 255u) == 0 && kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
+        ok = 0;
+        if (status) atomicExch(status, KF_DEV_TIMEOUT);
+        break;
+      }
+    }
+  }
+  if (threadIdx.x == 0) s_e = e;
+  ok = __syncthreads_and(ok);
+  MergeArgs a = m;
+  a.part_o = reinterpret_cast<const float*>(half);
+  a.part_lse = reinterpret_cast<const float*>(half + L.o_bytes);
+  a.S = world;
+  const int64_t row = blockIdx.x;
+  if (ok) {
+    merge_row<BF16>(a, row);
+  } else {
+    // a sender never published: NaN outputs instead of a partial merge
+    for (int c = threadIdx.x; c < a.D; c += blockDim.x) a.o[row * a.os0 + c] = 0x7fffu;
+    if (threadIdx.x == 0 && a.lse) a.lse[row] = __int_as_float(0x7fc00000);
+  }
+  // every CTA has read the epoch before the last one takes its ticket
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ctrl + 1, 1u) == gridDim.x - 1) {
+      ctrl[1] = 0;
+      __threadfence();
+      *reinterpret_cast<volatile uint32_t*>(ctrl) = s_e;
+    }
+  }
+}
+
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddrRangeFn get_addr_range_fn() {
+  static AddrRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddrRangeFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+extern "C" size_t kf_peer_mailbox_bytes(int world, int64_t rows, int64_t D) {
+  if (world <= 0 || world > kMaxPeers || rows <= 0 || D <= 0) return 0;
+  return (size_t)(256 + 2 * peer_layout(world, rows, (int)D).half);
+}
+
+extern "C" int kf_ipc_get_handle(const void* ptr, void* handle, uint64_t* offset) {
+  using kf::set_error;
+  if (!ptr || !handle || !offset) return set_error(KF_ERR_INVALID, "kf_ipc_get_handle: null argument");
+  AddrRangeFn range = get_addr_range_fn();
+  if (!range) return set_error(KF_ERR_CUDA, "kf_ipc_get_handle: cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return set_error(KF_ERR_INVALID, "kf_ipc_get_handle: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(KF_ERR_CUDA, "kf_ipc_get_handle: %s (the allocation must come from cudaMalloc)",
+                     cudaGetErrorString(err));
+  }
+  memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<uint64_t>(ptr) - (uint64_t)base;
+  return KF_OK;
+}
+
+extern "C" int kf_ipc_open_handle(const void* handle, uint64_t offset, void** ptr) {
+  using kf::set_error;
+  if (!handle || !ptr) return set_error(KF_ERR_INVALID, "kf_ipc_open_handle: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(KF_ERR_CUDA, "kf_ipc_open_handle: %s", cudaGetErrorString(err));
+  }
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return KF_OK;
+}
+
+extern "C" int kf_ipc_close_handle(void* ptr, uint64_t offset) {
+  if (!ptr) return kf::set_error(KF_ERR_INVALID, "kf_ipc_close_handle: null pointer");
+  const cudaError_t err = cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kf::set_error(KF_ERR_CUDA, "kf_ipc_close_handle: %s", cudaGetErrorString(err));
+  }
+  return KF_OK;
+}
+
+namespace {
+
+int check_peer_shape(const char* what, int64_t rows, int64_t D, int dtype, int world) {
+  if (world < 1 || world > kMaxPeers)
+    return kf::set_error(KF_ERR_INVALID, "%s: need 1 <= world <= %d", what, kMaxPeers);
+  if (rows <= 0 || rows > 0x7fffffffLL || D < 8 || D > 128 || D % 8)
+    return kf::set_error(KF_ERR_INVALID, "%s: need rows > 0 and D a multiple of 8 in [8, 128]", what);
+  if (dtype != KF_F16 && dtype != KF_BF16)
+    return kf::set_error(KF_ERR_INVALID, "%s: dtype must be fp16 or bf16", what);
+  return KF_OK;
+}
+
+bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
+}  // namespace
+
+extern "C" int kf_decode_peer_put(const void* o, const float* lse, int64_t rows, int64_t D, int dtype,
+                                  void* const* mailboxes, int world, int rank, void* stream) {
+  using kf::set_error;
+  if (!o || !lse || !mailboxes) return set_error(KF_ERR_INVALID, "kf_decode_peer_put: null argument");
+  int rc = check_peer_shape("kf_decode_peer_put", rows, D, dtype, world);
+  if (rc) return rc;
+  if (rank < 0 || rank >= world) return set_error(KF_ERR_INVALID, "kf_decode_peer_put: need 0 <= rank < world");
+  if (misaligned(o, 16) || misaligned(lse, 4)) return set_error(KF_ERR_INVALID, "kf_decode_peer_put: misaligned buffers");
+  PeerSet peers = {};
+  for (int r = 0; r < world; ++r) {
+    peers.mailbox[r] = static_cast<uint8_t*>(mailboxes[r]);
+    if (!peers.mailbox[r] || misaligned(peers.mailbox[r], 256))
+      return set_error(KF_ERR_INVALID, "kf_decode_peer_put: mailboxes must be 256-byte aligned");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(peer_layout(world, rows, (int)D).chunks, world);
+  if (dtype == KF_BF16)
+    peer_put_kernel<true><<<grid, kPeerThreads, 0, st>>>(static_cast<const uint16_t*>(o), lse, rows, (int)D, peers,
+                                                         world, rank);
+  else
+    peer_put_kernel<false><<<grid, kPeerThreads, 0, st>>>(static_cast<const uint16_t*>(o), lse, rows, (int)D, peers,
+                                                          world, rank);
+  return kf::check_launch("kf_decode_peer_put");
+}
+
+extern "C" int kf_decode_peer_merge(void* mailbox, int64_t rows, int64_t D, int dtype, int world, void* out,
+                                    float* out_lse, int32_t* status, void* stream) {
+  using kf::set_error;
+  if (!mailbox || !out) return set_error(KF_ERR_INVALID, "kf_decode_peer_merge: null argument");
+  int rc = check_peer_shape("kf_decode_peer_merge", rows, D, dtype, world);
+  if (rc) return rc;
+  if (misaligned(mailbox, 256) || misaligned(out, 8) || misaligned(out_lse, 4))
+    return set_error(KF_ERR_INVALID, "kf_decode_peer_merge: misaligned buffers");
+  MergeArgs m = {};
+  m.rows = rows;
+  m.D = (int)D;
+  m.o = static_cast<uint16_t*>(out);
+  m.lse = out_lse;
+  m.Hq = 1;
+  m.Sq = 1;
+  m.os0 = D;
+  m.S = world;
+  const int groups = kMergeThreads / ((int)D / 4);
+  const size_t smem = (size_t)(((world + 3) & ~3) + groups * D) * sizeof(float);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* mb = static_cast<uint8_t*>(mailbox);
+  if (dtype == KF_BF16)
+    return launch_dependent(peer_merge_kernel<true>, dim3((unsigned)rows), dim3(kMergeThreads), smem, st,
+                            "kf_decode_peer_merge", m, mb, world, status);
+  return launch_dependent(peer_merge_kernel<false>, dim3((unsigned)rows), dim3(kMergeThreads), smem, st,
+                          "kf_decode_peer_merge", m, mb, world, status);
+}
+
+extern "C" int kf_decode_peer_exchange(const void* o, const float* lse, int64_t rows, int64_t D,
+                                       int dtype, void* const* mailboxes, int world, int rank,
+                                       void* out, float* out_lse, int32_t* status, void* stream) {
+  if (!mailboxes || rank < 0 || rank >= world || world > kMaxPeers)
+    return kf::set_error(KF_ERR_INVALID, "kf_decode_peer_exchange: need mailboxes and 0 <= rank < world <= %d",
+                         kMaxPeers);
+  int rc = kf_decode_peer_put(o, lse, rows, D, dtype, mailboxes, world, rank, stream);
+  if (rc) return rc;
+  return kf_decode_peer_merge(mailboxes[rank], rows, D, dtype, world, out, out_lse, status, stream);
 }

@@ -14,10 +14,14 @@ allows:
   kernel, one all-gather exchanges the packed partials
   ``[B, Hq, Sq, D + 1]`` (fp32), and every rank merges them with the
   LSE-weighted merge kernel (the same math as the reference's split-KV
-  reduce, triton_forward.py:287-349).
+  reduce, triton_forward.py:287-349).  ``PeerExchange`` replaces the
+  all-gather + merge by two kernels over NVLink peer memory: each rank stores
+  its partial straight into every peer's mailbox and merges what arrives in
+  its own.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import List, Sequence, Tuple
 
 import torch
@@ -87,15 +91,114 @@ def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor, out_shape, dtyp
     return out, lse
 
 
+class PeerExchange:
+    """Mailboxes in every rank's GPU memory, mapped by all ranks of one box.
+
+    ``exchange(o, lse)`` sends this rank's partial ``o`` ([..., D], fp16/bf16)
+    and ``lse`` (fp32, natural log) to every rank and returns the LSE merge of
+    all ranks' partials (``kf_decode_peer_exchange``).  Every rank must call it
+    in the same order with the same shapes; the call count lives in device
+    memory, so the call may be captured in a CUDA graph.  A bounded wait
+    (about one second) guards every arrival: on expiry the output is NaN and
+    ``status()`` reports it, after which the exchange must be rebuilt.
+
+    Build it after ``init_process_group`` (it all-gathers the CUDA IPC
+    handles); with no process group it is a one-rank exchange.  The mailbox
+    comes from the caching allocator and needs plain ``cudaMalloc`` memory
+    (not ``expandable_segments``).
+    """
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, rows: int, d: int, dtype: torch.dtype, device=None, group=None):
+        self.lib = _ext.load()
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        if dist.is_available() and dist.is_initialized():
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        self.rows, self.d, self.dtype = int(rows), int(d), dtype
+        self.dtype_code = _ext.dtype_code(dtype)
+        nbytes = self.lib.kf_peer_mailbox_bytes(self.world, self.rows, self.d)
+        if nbytes == 0:
+            raise ValueError(f"PeerExchange: unsupported world={self.world} rows={rows} d={d}")
+        self.mailbox = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
+        base = self.mailbox.data_ptr()
+        self.local = (base + 255) // 256 * 256
+        self.status_word = torch.zeros(1, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)  # zeros land before any peer can write
+        handle = (ctypes.c_uint8 * self.HANDLE_BYTES)()
+        offset = ctypes.c_uint64(0)
+        _ext.check(self.lib.kf_ipc_get_handle(ctypes.c_void_p(self.local), handle, ctypes.byref(offset)),
+                   "kf_ipc_get_handle")
+        mine = (bytes(handle), int(offset.value))
+        if self.world > 1:
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        self._opened = []
+        ptrs = []
+        for r, (h, off) in enumerate(allh):
+            if r == self.rank:
+                ptrs.append(self.local)
+                continue
+            hb = (ctypes.c_uint8 * self.HANDLE_BYTES).from_buffer_copy(h)
+            p = ctypes.c_void_p()
+            _ext.check(self.lib.kf_ipc_open_handle(hb, ctypes.c_uint64(off), ctypes.byref(p)),
+                       "kf_ipc_open_handle")
+            self._opened.append((p.value, off))
+            ptrs.append(p.value)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        if self.world > 1:
+            dist.barrier(group=group)  # every rank mapped every mailbox
+
+    def exchange(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor = None,
+                 out_lse: torch.Tensor = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        if o.dtype != self.dtype or o.shape[-1] != self.d or o[..., 0].numel() != self.rows:
+            raise ValueError("PeerExchange.exchange: o does not match the exchange's rows/d/dtype")
+        if lse.numel() != self.rows or lse.dtype != torch.float32:
+            raise ValueError("PeerExchange.exchange: lse must be fp32 with one value per row")
+        o = o.contiguous()
+        lse = lse.contiguous()
+        if out is None:
+            out = torch.empty_like(o)
+        if out_lse is None:
+            out_lse = torch.empty(lse.shape, dtype=torch.float32, device=o.device)
+        rc = self.lib.kf_decode_peer_exchange(o.data_ptr(), lse.data_ptr(), self.rows, self.d,
+                                              self.dtype_code, self.ptrs, self.world, self.rank,
+                                              out.data_ptr(), out_lse.data_ptr(),
+                                              self.status_word.data_ptr(), _ext.stream_of(o))
+        _ext.check(rc, "kf_decode_peer_exchange")
+        return out, out_lse
+
+    def status(self) -> int:
+        """KF_DEV_TIMEOUT (1) once a wait expired, else 0 (synchronises)."""
+        return int(self.status_word.item())
+
+    def close(self) -> None:
+        """Unmap the peers' mailboxes (every rank, after its last exchange)."""
+        torch.cuda.synchronize(self.device)
+        for p, off in self._opened:
+            self.lib.kf_ipc_close_handle(ctypes.c_void_p(p), ctypes.c_uint64(off))
+        self._opened = []
+
+
 def decode_kv_split(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, *,
-                    scale: float, group=None) -> Tuple[torch.Tensor, torch.Tensor]:
+                    scale: float, group=None,
+                    exchange: PeerExchange = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Decode over a KV sequence split across ranks; every rank returns the full (O, LSE).
 
     ``k_local``/``v_local`` hold this rank's contiguous key chunk (see
-    ``kv_chunk``).  One NCCL all-gather of the packed partials, then the merge.
+    ``kv_chunk``).  With ``exchange`` (a ``PeerExchange`` built for
+    ``B * Hq * Sq`` rows) the partials cross NVLink through peer memory;
+    otherwise one NCCL all-gather of the packed partials, then the merge.
     """
     from .attention import _decode_forward
 
     o, lse = _decode_forward(q, k_local, v_local, scale=scale, want_lse=True)
+    if exchange is not None:
+        return exchange.exchange(o, lse)
     part_o, part_lse = gather_partials(pack_partial(o, lse), group)
     return merge_partials(part_o, part_lse, tuple(q.shape), q.dtype)
