@@ -154,29 +154,46 @@ int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits
  * maps every peer's through CUDA IPC: kf_ipc_get_handle gives a 64-byte
  * handle plus the pointer's offset inside its allocation, kf_ipc_open_handle
  * maps a peer's handle in this process, kf_ipc_close_handle unmaps it.
+ * mailboxes[r] is rank r's mailbox as mapped here (mailboxes[rank] is the
+ * local one).  1 <= world <= 8; D a multiple of 8 in [8, 128].
  *
- * kf_decode_peer_exchange: o [rows, D] (fp16/bf16, this rank's normalised
- * partial output, contiguous) and lse [rows] fp32 (natural log) are sent to
- * every rank with plain peer stores and a system-scope release flag; the
- * second kernel waits until all `world` partials of this call have arrived
- * in this rank's mailbox (bounded: about one second, then *status =
- * KF_DEV_TIMEOUT and out = NaN) and writes the LSE merge into out [rows, D]
- * and out_lse [rows] (may be null).  mailboxes[r] is rank r's mailbox as
- * mapped here (mailboxes[rank] is the local one).  Every rank must make the
- * same sequence of calls with the same rows and D (the call count is kept
- * in the mailbox, so the two launches may be captured in a CUDA graph and
- * replayed).  1 <= world <= 8; D a multiple of 8 in [8, 128].  After a
- * timeout the mailboxes must be zeroed on every rank before the next call.
+ * kf_decode_kv_split_peer: split-KV decode of this rank's key chunk (q, k, v
+ * as kf_decode, no fused append; rows = B*Hq*Sq) fused with the exchange:
+ * the split kernel, a kernel that merges this rank's splits and stores the
+ * fp32 result into every mailbox (peer stores, then a system-scope release
+ * add on the receiver's arrival counter), and the final merge into o / lse
+ * (lse may be null).  num_splits >= 1 (the plan's value); the workspace
+ * needs kf_decode_workspace_bytes(B, Hq, Sq, D, max(2, num_splits)) bytes.
+ * kf_decode_kv_split_peer_send is its first two kernels alone (nothing
+ * waits); kf_decode_peer_merge with rows = B*Hq*Sq then gives the result
+ * as a contiguous [rows, D].
  *
+ * kf_decode_peer_exchange: the same exchange for a finished partial: o
+ * [rows, D] (fp16/bf16, normalised, contiguous) and lse [rows] fp32 (natural
+ * log) in, the merge of all ranks' partials out ([rows, D] and [rows]).
  * kf_decode_peer_put / kf_decode_peer_merge are its two halves.  The put
- * never waits; the merge waits for the flags of all `world` puts of the
- * current call, so a single process may drive several mailboxes on one GPU
- * (all puts first, then the merges) without kernels that wait on one
- * another. */
+ * never waits; the merge waits for all `world` partials of the current call,
+ * so a single process may drive several mailboxes on one GPU (all puts
+ * first, then the merges) without kernels that wait on one another.
+ *
+ * Every wait is bounded (about one second): on expiry *status (device
+ * memory, may be null) = KF_DEV_TIMEOUT and the output is NaN; the mailboxes
+ * must then be zeroed on every rank before the next call.  Every rank must
+ * make the same sequence of calls with the same rows and D; the call count
+ * is kept in the mailbox, so the launches may be captured in a CUDA graph
+ * and replayed. */
 size_t kf_peer_mailbox_bytes(int world, int64_t rows, int64_t D);
 int kf_ipc_get_handle(const void* ptr, void* handle64, uint64_t* offset);
 int kf_ipc_open_handle(const void* handle64, uint64_t offset, void** ptr);
 int kf_ipc_close_handle(void* ptr, uint64_t offset);
+int kf_decode_kv_split_peer(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                            const kf_tensor4* o, float* lse, int dtype, float scale, int num_splits,
+                            void* workspace, size_t workspace_bytes, void* const* mailboxes,
+                            int world, int rank, int32_t* status, void* stream);
+int kf_decode_kv_split_peer_send(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                                 int dtype, float scale, int num_splits, void* workspace,
+                                 size_t workspace_bytes, void* const* mailboxes, int world, int rank,
+                                 void* stream);
 int kf_decode_peer_exchange(const void* o, const float* lse, int64_t rows, int64_t D,
                             int dtype, void* const* mailboxes, int world, int rank,
                             void* out, float* out_lse, int32_t* status, void* stream);

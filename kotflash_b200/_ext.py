@@ -75,6 +75,8 @@ SIGNATURES = {
     "kf_decode_peer_exchange": (_I, [_VP, _VP, _I64, _I64, _I, _VP, _I, _I, _VP, _VP, _VP, _VP]),
     "kf_decode_peer_put": (_I, [_VP, _VP, _I64, _I64, _I, _VP, _I, _I, _VP]),
     "kf_decode_peer_merge": (_I, [_VP, _I64, _I64, _I, _I, _VP, _VP, _VP, _VP]),
+    "kf_decode_kv_split_peer": (_I, [_T4, _T4, _T4, _T4, _VP, _I, _F, _I, _VP, _SZ, _VP, _I, _I, _VP, _VP]),
+    "kf_decode_kv_split_peer_send": (_I, [_T4, _T4, _T4, _I, _F, _I, _VP, _SZ, _VP, _I, _I, _VP]),
 }
 
 _load_lock = threading.Lock()

@@ -53,6 +53,7 @@ struct DecodeArgs {
   int B, Hq, Hkv, G, Sq, Sk, D;
   int64_t past_len;
   int num_splits, chunk;
+  bool direct;  // one split writing O/LSE itself; otherwise fp32 partials for a merge
   int rows;  // G * Sq packed rows per KV head
   int64_t prow_total;  // B * Hq * Sq
   float scale_log2;
@@ -416,7 +417,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     const int64_t pbase = (int64_t)(b * a.Hkv + kvh) * a.rows + row0;
     for (int i = tid; i < valid * a.D; i += kThreads) {
       const int r = i / a.D, c = i % a.D, pr = row0 + r;
-      if (a.num_splits == 1) {
+      if (a.direct) {
         a.o[b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2] + c] = 0x7fffu;
       } else {
         a.part_o[((int64_t)split * a.prow_total + pbase + r) * a.D + c] = __int_as_float(0x7fc00000);
@@ -494,7 +495,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
       for (int e = 0; e < 4; ++e) acc[e] += wt * obuf[(w * ROWS + r) * DP + c4 + e];
     }
     const int pr = row0 + r;
-    if (a.num_splits == 1) {
+    if (a.direct) {
       const int g = pr / a.Sq, s = pr % a.Sq;
       uint16_t* dst = a.o + b * a.os[0] + (int64_t)(kvh * a.G + g) * a.os[1] + s * a.os[2] + c4;
       const uint32_t lo = kf::pack2<BF16>(acc[0], acc[1]), hi = kf::pack2<BF16>(acc[2], acc[3]);
@@ -505,7 +506,7 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     }
   }
   if (tid < valid_rows) {
-    if (a.num_splits == 1) {
+    if (a.direct) {
       if (a.lse) a.lse[prow_base + tid] = row_lse[tid];
     } else {
       a.part_lse[(int64_t)split * a.prow_total + prow_base + tid] = row_lse[tid];
@@ -756,7 +757,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
           kf::tmem_ld16(lane_base + 128 + c0, ov);
           kf::tmem_wait_ld();
           if (!row_ok) continue;
-          if (a.num_splits == 1) {
+          if (a.direct) {
             uint16_t* dst = a.o + b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2];
 #pragma unroll
             for (int c = 0; c < 16; c += 2)
@@ -774,7 +775,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
           }
         }
         if (row_ok) {
-          if (a.num_splits == 1) {
+          if (a.direct) {
             if (a.lse) a.lse[prow] = row_lse;
           } else {
             a.part_lse[(int64_t)split * a.prow_total + prow] = row_lse;
@@ -788,12 +789,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
       if (r < valid_rows) {
         const int64_t prow = (int64_t)(b * a.Hkv + kvh) * a.rows + pr;
         for (int c = 0; c < a.D; ++c) {
-          if (a.num_splits == 1)
+          if (a.direct)
             a.o[b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2] + c] = 0x7fffu;
           else
             a.part_o[((int64_t)split * a.prow_total + prow) * a.D + c] = __int_as_float(0x7fc00000);
         }
-        if (a.num_splits > 1) a.part_lse[(int64_t)split * a.prow_total + prow] = 0.f;
+        if (!a.direct) a.part_lse[(int64_t)split * a.prow_total + prow] = 0.f;
       }
     }
   }
@@ -828,8 +829,10 @@ struct MergeArgs {
 constexpr int kMergeThreads = 256;
 constexpr int kMergeBatch = 8;  // partial loads in flight per thread
 
-template <bool BF16>
-__device__ __forceinline__ void merge_row(const MergeArgs& a, const int64_t row) {
+// The merged row goes to out(c4, o4, lse): thread c4 < D/4 holds columns
+// [4 c4, 4 c4 + 4), normalised; every such thread also gets the row's LSE.
+template <class Out>
+__device__ __forceinline__ void merge_row_to(const MergeArgs& a, const int64_t row, Out&& out) {
   extern __shared__ float sm[];          // [S] weights, then [G][D] partial sums
   float* wts = sm;
   float* part = sm + ((a.S + 3) & ~3);
@@ -919,14 +922,22 @@ __device__ __forceinline__ void merge_row(const MergeArgs& a, const int64_t row)
       acc[2] += p.z;
       acc[3] += p.w;
     }
+    out(tid, make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv),
+        den > 0.f ? mx + logf(den) : -INFINITY);
+  }
+}
+
+// Output row `row` of a.o (strided [B, Hq, Sq, D]) and a.lse.
+template <bool BF16>
+__device__ __forceinline__ void merge_row(const MergeArgs& a, const int64_t row) {
+  merge_row_to(a, row, [&](int c4, float4 v, float l) {
     const int64_t bh = row / a.Sq;
     const int64_t s_ = row % a.Sq;
     const int64_t b_ = bh / a.Hq, h_ = bh % a.Hq;
-    uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + tid * 4;
-    const uint32_t lo = kf::pack2<BF16>(acc[0] * inv, acc[1] * inv), hi = kf::pack2<BF16>(acc[2] * inv, acc[3] * inv);
-    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-    if (tid == 0 && a.lse) a.lse[row] = den > 0.f ? mx + logf(den) : -INFINITY;
-  }
+    uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + c4 * 4;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(kf::pack2<BF16>(v.x, v.y), kf::pack2<BF16>(v.z, v.w));
+    if (c4 == 0 && a.lse) a.lse[row] = l;
+  });
 }
 
 template <bool BF16>
@@ -1085,54 +1096,58 @@ extern "C" size_t kf_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, i
   return (size_t)num_splits * (size_t)(B * Hq * Sq) * (size_t)(D + 1) * sizeof(float) + 256;
 }
 
-extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
-                         const kf_tensor4* new_k, const kf_tensor4* new_v, int64_t past_len,
-                         const kf_tensor4* o, float* lse, int dtype, float scale, int num_splits,
-                         void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+
+// Validates the descriptors and fills `a`: split geometry and, when the
+// splits write fp32 partials (more than one split, or `partials` forced), the
+// workspace carve-up.  Messages are prefixed with `what`.
+int decode_setup(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const kf_tensor4* new_k,
+                 const kf_tensor4* new_v, int64_t past_len, const kf_tensor4* o, float* lse, int dtype,
+                 float scale, int num_splits, void* workspace, size_t workspace_bytes, bool partials,
+                 const char* what, DecodeArgs& a) {
   using kf::set_error;
-  if (!q || !k || !v || !o) return set_error(KF_ERR_INVALID, "kf_decode: null tensor descriptor");
+  if (!q || !k || !v || !o) return set_error(KF_ERR_INVALID, "%s: null tensor descriptor", what);
   if (dtype != KF_F16 && dtype != KF_BF16)
-    return set_error(KF_ERR_INVALID, "kf_decode: dtype must be fp16 or bf16");
+    return set_error(KF_ERR_INVALID, "%s: dtype must be fp16 or bf16", what);
   const int64_t B = q->size[0], Hq = q->size[1], Sq = q->size[2], D = q->size[3];
   const int64_t Hkv = k->size[1], Sk = k->size[2];
   for (int i = 0; i < 4; ++i)
-    if (k->size[i] != v->size[i]) return set_error(KF_ERR_INVALID, "kf_decode: K and V shapes must match");
+    if (k->size[i] != v->size[i]) return set_error(KF_ERR_INVALID, "%s: K and V shapes must match", what);
   if (k->size[0] != B || k->size[3] != D)
-    return set_error(KF_ERR_INVALID, "kf_decode: K/V batch and head_dim must match Q");
+    return set_error(KF_ERR_INVALID, "%s: K/V batch and head_dim must match Q", what);
   for (int i = 0; i < 4; ++i)
-    if (o->size[i] != q->size[i]) return set_error(KF_ERR_INVALID, "kf_decode: O must have Q's shape");
+    if (o->size[i] != q->size[i]) return set_error(KF_ERR_INVALID, "%s: O must have Q's shape", what);
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0)
-    return set_error(KF_ERR_INVALID, "kf_decode: dimensions must be non-zero");
+    return set_error(KF_ERR_INVALID, "%s: dimensions must be non-zero", what);
   if (Hq % Hkv != 0)
-    return set_error(KF_ERR_INVALID, "kf_decode: num_query_heads must be divisible by num_kv_heads");
-  if (Sq > 16) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: Sq must be <= 16");
+    return set_error(KF_ERR_INVALID, "%s: num_query_heads must be divisible by num_kv_heads", what);
+  if (Sq > 16) return set_error(KF_ERR_UNSUPPORTED, "%s: Sq must be <= 16", what);
   if (D < 16 || D > 128 || D % 8 != 0)
-    return set_error(KF_ERR_UNSUPPORTED, "kf_decode: head_dim must be a multiple of 8 in [16, 128]");
-  if (Sk > (int64_t)1 << 30) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: Sk too large");
+    return set_error(KF_ERR_UNSUPPORTED, "%s: head_dim must be a multiple of 8 in [16, 128]", what);
+  if (Sk > (int64_t)1 << 30) return set_error(KF_ERR_UNSUPPORTED, "%s: Sk too large", what);
   if (!rows16(q) || !rows16(k) || !rows16(v) || !rows16(o))
-    return set_error(KF_ERR_INVALID,
-                     "kf_decode: tensors need a contiguous last dim and 16-byte aligned rows");
+    return set_error(KF_ERR_INVALID, "%s: tensors need a contiguous last dim and 16-byte aligned rows", what);
   const bool fused = new_k != nullptr || new_v != nullptr;
   if (fused) {
-    if (!new_k || !new_v) return set_error(KF_ERR_INVALID, "kf_decode: new_k and new_v go together");
+    if (!new_k || !new_v) return set_error(KF_ERR_INVALID, "%s: new_k and new_v go together", what);
     if (new_k->size[0] != B || new_k->size[1] != Hkv || new_k->size[2] != 1 || new_k->size[3] != D)
-      return set_error(KF_ERR_INVALID, "kf_decode: new K/V must be [B, Hkv, 1, D]");
+      return set_error(KF_ERR_INVALID, "%s: new K/V must be [B, Hkv, 1, D]", what);
     for (int i = 0; i < 4; ++i)
       if (new_v->size[i] != new_k->size[i])
-        return set_error(KF_ERR_INVALID, "kf_decode: new K and V shapes must match");
+        return set_error(KF_ERR_INVALID, "%s: new K and V shapes must match", what);
     if (!rows16(new_k) || !rows16(new_v))
-      return set_error(KF_ERR_INVALID, "kf_decode: new K/V rows must be 16-byte aligned");
+      return set_error(KF_ERR_INVALID, "%s: new K/V rows must be 16-byte aligned", what);
     if (past_len != Sk - 1)
-      return set_error(KF_ERR_INVALID, "kf_decode: fused append needs past_len == Sk - 1");
+      return set_error(KF_ERR_INVALID, "%s: fused append needs past_len == Sk - 1", what);
   }
   if (num_splits <= 0)
     num_splits = kf_decode_num_splits(B, Hq, Hkv, Sq, Sk, D, kf::sm_count_current_device());
-  if (num_splits > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many splits");
+  if (num_splits > 65535) return set_error(KF_ERR_UNSUPPORTED, "%s: too many splits", what);
   const int64_t tk = decode_tile_keys(Hq / Hkv * Sq, D, fused);
   const int64_t chunk = cdiv64(cdiv64(Sk, num_splits), tk) * tk;
   num_splits = (int)cdiv64(Sk, chunk);
 
-  DecodeArgs a;
+  a = DecodeArgs{};
   a.q = static_cast<const uint16_t*>(q->ptr);
   a.k = static_cast<const uint16_t*>(k->ptr);
   a.v = static_cast<const uint16_t*>(v->ptr);
@@ -1166,32 +1181,51 @@ extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tens
   a.part_o = nullptr;
   a.part_lse = nullptr;
   a.status = nullptr;
-  if (num_splits > 1) {
-    const size_t need = kf_decode_workspace_bytes(B, Hq, Sq, D, num_splits);
+  a.direct = num_splits == 1 && !partials;
+  if (!a.direct) {
+    const size_t need = (size_t)num_splits * (size_t)(B * Hq * Sq) * (size_t)(D + 1) * sizeof(float) + 256;
     if (!workspace || workspace_bytes < need)
-      return set_error(KF_ERR_WORKSPACE, "kf_decode: workspace needs %zu bytes", need);
+      return set_error(KF_ERR_WORKSPACE, "%s: workspace needs %zu bytes", what, need);
     uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255);
     a.part_o = reinterpret_cast<float*>(base);
     a.part_lse = a.part_o + (size_t)num_splits * a.prow_total * D;
   }
-  if (a.G * a.Sq > (1 << 20)) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: too many rows per KV head");
-  if ((int64_t)B * Hkv > 65535) return set_error(KF_ERR_UNSUPPORTED, "kf_decode: B*Hkv too large");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int rc = dtype == KF_BF16 ? dispatch_split<true>(a, k, v, st) : dispatch_split<false>(a, k, v, st);
-  if (rc != KF_OK || num_splits == 1) return rc;
+  if (a.G * a.Sq > (1 << 20)) return set_error(KF_ERR_UNSUPPORTED, "%s: too many rows per KV head", what);
+  if ((int64_t)B * Hkv > 65535) return set_error(KF_ERR_UNSUPPORTED, "%s: B*Hkv too large", what);
+  return KF_OK;
+}
+
+MergeArgs merge_args_of(const DecodeArgs& a) {
   MergeArgs m;
   m.part_o = a.part_o;
   m.part_lse = a.part_lse;
-  m.S = num_splits;
+  m.S = a.num_splits;
   m.rows = a.prow_total;
   m.D = a.D;
   m.o = a.o;
-  m.lse = lse;
+  m.lse = a.lse;
   m.Hq = a.Hq;
   m.Sq = a.Sq;
   m.os0 = a.os[0];
   m.os1 = a.os[1];
   m.os2 = a.os[2];
+  return m;
+}
+
+}  // namespace
+
+extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                         const kf_tensor4* new_k, const kf_tensor4* new_v, int64_t past_len,
+                         const kf_tensor4* o, float* lse, int dtype, float scale, int num_splits,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  DecodeArgs a;
+  int rc = decode_setup(q, k, v, new_k, new_v, past_len, o, lse, dtype, scale, num_splits, workspace,
+                        workspace_bytes, false, "kf_decode", a);
+  if (rc != KF_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = dtype == KF_BF16 ? dispatch_split<true>(a, k, v, st) : dispatch_split<false>(a, k, v, st);
+  if (rc != KF_OK || a.direct) return rc;
+  const MergeArgs m = merge_args_of(a);
   return dtype == KF_BF16 ? launch_merge<true>(m, st) : launch_merge<false>(m, st);
 }
 
@@ -1318,49 +1352,75 @@ extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const
 // merge of all of them.  Instead of a library all-gather followed by a merge
 // launch, each rank owns a mailbox in its own memory that every peer can
 // write (CUDA IPC mapping, peer access over NVLink/NVSwitch; no multicast):
-//   put:   CTA p stores this rank's partial (converted to fp32) into slot
-//          [rank] of rank p's mailbox with plain peer stores, then publishes
-//          it with a system-scope release store of the epoch into a flag;
-//   merge: every CTA waits (bounded) until all W flags of its own mailbox
-//          show the epoch, then merges the W partials (the split-merge math).
-// The epoch lives in the mailbox (advanced by the last merge CTA), so the
-// exchange works unchanged inside CUDA graphs; mailbox halves alternate by
-// epoch parity, and a rank cannot reach epoch e + 2 before every peer has
-// finished merging epoch e (its merge of e + 1 needs their put of e + 1,
-// which follows their merge of e in stream order).
+//   put:   this rank's partial rows are stored (fp32) into slot [rank] of
+//          every rank's mailbox with plain peer stores; after each piece the
+//          sender adds the piece's row count to the receiver's arrival
+//          counter with a system-scope release reduction;
+//   merge: every CTA waits (bounded) until its mailbox's counter shows all
+//          W x rows rows of this call, then merges the W partials (the
+//          split-merge math).
+// Two producers exist: kf_decode_peer_put sends a finished (O, LSE), and the
+// fused kv-split entry sends straight from the local merge of its splits
+// (one kernel less, and no rounding of the partial to fp16/bf16).
 //
+// The call count (epoch) lives in the mailbox and is advanced by the last
+// merge CTA, so the exchange works unchanged inside CUDA graphs.  Mailbox
+// halves alternate by epoch parity; a rank cannot write epoch e + 2 into a
+// half before every peer has finished merging epoch e from it (its merge of
+// e + 1 needs their rows of e + 1, sent after their merge of e in stream
+// order).  Counters only grow: after epoch e the counter of half (e & 1)
+// holds W * rows * ((e + 1) / 2) modulo 2^32, and no intermediate value of
+// an epoch equals it.
+//
+// Mailbox layout: [0, 256) control words {completed epochs, done ticket},
+// then two halves of {O [W][rows][D] fp32, LSE [W][rows] fp32, counter}.
 namespace {
 
-// Mailbox layout: [0, 256) control words {completed epochs, done ticket},
-// then two halves of {O [W][rows][D] fp32, LSE [W][rows] fp32,
-// flags [W][kPeerChunks]}.  Each sender's partial travels in up to
-// kPeerChunks pieces, one CTA and one flag each.
 constexpr int kMaxPeers = 8;
 constexpr int kPeerChunks = 16;
 constexpr int kPeerThreads = 256;
 
 struct PeerLayout {
-  int64_t o_bytes, lse_bytes, flag_bytes, half;
-  int chunks;  // pieces per sender: same on every rank (depends on rows and D only)
+  int64_t o_bytes, lse_bytes, half;
 };
 
 __host__ __device__ inline PeerLayout peer_layout(int world, int64_t rows, int D) {
   PeerLayout L;
   L.o_bytes = ((int64_t)world * rows * D * 4 + 255) & ~int64_t(255);
   L.lse_bytes = ((int64_t)world * rows * 4 + 255) & ~int64_t(255);
-  L.flag_bytes = ((int64_t)world * kPeerChunks * 4 + 255) & ~int64_t(255);
-  L.half = L.o_bytes + L.lse_bytes + L.flag_bytes;
-  const int64_t pieces = (rows * D * 4 + 16383) / 16384;  // ~16 KB of fp32 O per CTA
-  L.chunks = (int)(pieces < 1 ? 1 : (pieces > kPeerChunks ? kPeerChunks : pieces));
+  L.half = L.o_bytes + L.lse_bytes + 256;
   return L;
+}
+
+// Rows per piece of kf_decode_peer_put (~16 KB of fp32 O per CTA, at most kPeerChunks pieces).
+inline int64_t put_rows_per_piece(int64_t rows, int D) {
+  int64_t pieces = (rows * D * 4 + 16383) / 16384;
+  pieces = pieces < 1 ? 1 : (pieces > kPeerChunks ? kPeerChunks : pieces);
+  return (rows + pieces - 1) / pieces;
 }
 
 struct PeerSet {
   uint8_t* mailbox[kMaxPeers];  // every rank's mailbox base, this rank's own included
 };
 
-KF_DEVI void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+struct PeerHalf {
+  float* o;
+  float* lse;
+  uint32_t* counter;
+};
+
+KF_DEVI PeerHalf peer_half(uint8_t* mailbox, const PeerLayout& L, uint32_t e) {
+  uint8_t* h = mailbox + 256 + (e & 1) * L.half;
+  return {reinterpret_cast<float*>(h), reinterpret_cast<float*>(h + L.o_bytes),
+          reinterpret_cast<uint32_t*>(h + L.o_bytes + L.lse_bytes)};
+}
+
+KF_DEVI uint32_t current_epoch(const uint8_t* mailbox) {
+  return *reinterpret_cast<const volatile uint32_t*>(mailbox) + 1;
+}
+
+KF_DEVI void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 KF_DEVI uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -1368,55 +1428,76 @@ KF_DEVI uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// grid (chunks, world): CTA (c, p) sends piece c of this rank's partial to rank p.
+// grid (pieces, world): CTA (c, p) sends rows [c * rpp, (c + 1) * rpp) of this rank's partial to rank p.
 template <bool BF16>
 __global__ void __launch_bounds__(kPeerThreads) peer_put_kernel(const uint16_t* o, const float* lse, int64_t rows,
-                                                                int D, const __grid_constant__ PeerSet peers,
-                                                                int world, int rank) {
-  kf::griddep_launch_dependents();  // the merge may launch now; it waits for the flags, not for this grid
+                                                                int D, int64_t rpp,
+                                                                const __grid_constant__ PeerSet peers, int world,
+                                                                int rank) {
+  kf::griddep_launch_dependents();  // the merge may launch now; it waits for the counter, not for this grid
   const PeerLayout L = peer_layout(world, rows, D);
-  const uint32_t* ctrl = reinterpret_cast<const uint32_t*>(peers.mailbox[rank]);
-  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(ctrl) + 1;
-  uint8_t* half = peers.mailbox[blockIdx.y] + 256 + (e & 1) * L.half;
-  float* dst_o = reinterpret_cast<float*>(half) + (int64_t)rank * rows * D;
-  float* dst_lse = reinterpret_cast<float*>(half + L.o_bytes) + (int64_t)rank * rows;
-  uint32_t* flag = reinterpret_cast<uint32_t*>(half + L.o_bytes + L.lse_bytes) + rank * kPeerChunks + blockIdx.x;
-  const int64_t n8 = rows * D / 8;  // D % 8 == 0
-  const int64_t per = (n8 + L.chunks - 1) / L.chunks;
-  const int64_t i0 = blockIdx.x * per, i1 = i0 + per < n8 ? i0 + per : n8;
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+  const uint32_t e = current_epoch(peers.mailbox[rank]);
+  const PeerHalf h = peer_half(peers.mailbox[blockIdx.y], L, e);
+  const int64_t r0 = blockIdx.x * rpp, r1 = r0 + rpp < rows ? r0 + rpp : rows;
+  if (r0 >= r1) return;
+  float* dst_o = h.o + (int64_t)rank * rows * D;
+  const int64_t per_row = D / 8;  // D % 8 == 0
+  for (int64_t i = r0 * per_row + threadIdx.x; i < r1 * per_row; i += blockDim.x) {
     const uint4 v = reinterpret_cast<const uint4*>(o)[i];
     const float2 f0 = kf::unpack2<BF16>(v.x), f1 = kf::unpack2<BF16>(v.y);
     const float2 f2 = kf::unpack2<BF16>(v.z), f3 = kf::unpack2<BF16>(v.w);
     reinterpret_cast<float4*>(dst_o)[2 * i] = make_float4(f0.x, f0.y, f1.x, f1.y);
     reinterpret_cast<float4*>(dst_o)[2 * i + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
   }
-  if (blockIdx.x == 0)
-    for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) dst_lse[i] = lse[i];
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) h.lse[(int64_t)rank * rows + r] = lse[r];
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    st_release_sys(flag, e);
+    red_release_sys_add(h.counter, (uint32_t)(r1 - r0));
   }
 }
 
-// grid rows: waits (bounded) for every sender's pieces of this epoch, merges
-// one row, and the last CTA advances the epoch.
+// grid rows: merges the local split partials of one row (as merge_kernel) and
+// sends the fp32 result to slot [rank] of every rank's mailbox.
+__global__ void __launch_bounds__(kMergeThreads) merge_put_kernel(const MergeArgs a,
+                                                                  const __grid_constant__ PeerSet peers,
+                                                                  int world, int rank) {
+  kf::griddep_wait();  // partials of the split kernel
+  kf::griddep_launch_dependents();
+  const PeerLayout L = peer_layout(world, a.rows, a.D);
+  const uint32_t e = current_epoch(peers.mailbox[rank]);
+  const int64_t row = blockIdx.x;
+  const int64_t slot = (int64_t)rank * a.rows + row;
+  merge_row_to(a, row, [&](int c4, float4 v, float l) {
+    for (int p = 0; p < world; ++p) {
+      const PeerHalf h = peer_half(peers.mailbox[p], L, e);
+      *reinterpret_cast<float4*>(h.o + slot * a.D + c4 * 4) = v;
+      if (c4 == 0) h.lse[slot] = l;
+    }
+  });
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < world; ++p) red_release_sys_add(peer_half(peers.mailbox[p], L, e).counter, 1u);
+  }
+}
+
+// grid rows: waits (bounded) until all W x rows rows of this epoch arrived,
+// merges one row, and the last CTA advances the epoch.
 template <bool BF16>
 __global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(MergeArgs m, uint8_t* mailbox,
                                                                     int world, int32_t* status) {
-  static_assert(kMergeThreads >= kMaxPeers * kPeerChunks, "one flag per thread");
-  __shared__ uint32_t s_e;
+  __shared__ int s_ok;
   const PeerLayout L = peer_layout(world, m.rows, m.D);
   uint32_t* ctrl = reinterpret_cast<uint32_t*>(mailbox);
-  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctrl) + 1;
-  const uint8_t* half = mailbox + 256 + (e & 1) * L.half;
-  int ok = 1;
-  if (threadIdx.x < world * kPeerChunks && (int)(threadIdx.x % kPeerChunks) < L.chunks) {
-    const uint32_t* flag = reinterpret_cast<const uint32_t*>(half + L.o_bytes + L.lse_bytes) + threadIdx.x;
+  const uint32_t e = current_epoch(mailbox);
+  const PeerHalf h = peer_half(mailbox, L, e);
+  if (threadIdx.x == 0) {
+    const uint32_t target = (uint32_t)world * (uint32_t)m.rows * ((e + 1) >> 1);
+    int ok = 1;
     const uint64_t t0 = kf::global_timer_ns();
     uint32_t spins = 0;
-    while (ld_acquire_sys(flag) != e) {
+    while (ld_acquire_sys(h.counter) != target) {
       __nanosleep(32);
       if ((++spins & 255u) == 0 && kf::global_timer_ns() - t0 > kf::kWaitBudgetNs) {
         ok = 0;
@@ -1424,20 +1505,24 @@ __global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(MergeArgs m, 
         break;
       }
     }
+    s_ok = ok;
   }
-  if (threadIdx.x == 0) s_e = e;
-  ok = __syncthreads_and(ok);
+  __syncthreads();
   MergeArgs a = m;
-  a.part_o = reinterpret_cast<const float*>(half);
-  a.part_lse = reinterpret_cast<const float*>(half + L.o_bytes);
+  a.part_o = h.o;
+  a.part_lse = h.lse;
   a.S = world;
   const int64_t row = blockIdx.x;
-  if (ok) {
+  if (s_ok) {
     merge_row<BF16>(a, row);
   } else {
-    // a sender never published: NaN outputs instead of a partial merge
-    for (int c = threadIdx.x; c < a.D; c += blockDim.x) a.o[row * a.os0 + c] = 0x7fffu;
-    if (threadIdx.x == 0 && a.lse) a.lse[row] = __int_as_float(0x7fc00000);
+    // a sender never arrived: NaN outputs instead of a partial merge
+    merge_row_to(a, row, [&](int c4, float4, float) {
+      const int64_t bh = row / a.Sq, s_ = row % a.Sq, b_ = bh / a.Hq, h_ = bh % a.Hq;
+      uint16_t* dst = a.o + b_ * a.os0 + h_ * a.os1 + s_ * a.os2 + c4 * 4;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(0x7fff7fffu, 0x7fff7fffu);
+      if (c4 == 0 && a.lse) a.lse[row] = __int_as_float(0x7fc00000);
+    });
   }
   // every CTA has read the epoch before the last one takes its ticket
   __syncthreads();
@@ -1446,7 +1531,7 @@ __global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(MergeArgs m, 
     if (atomicAdd(ctrl + 1, 1u) == gridDim.x - 1) {
       ctrl[1] = 0;
       __threadfence();
-      *reinterpret_cast<volatile uint32_t*>(ctrl) = s_e;
+      *reinterpret_cast<volatile uint32_t*>(ctrl) = e;
     }
   }
 }
@@ -1464,6 +1549,42 @@ AddrRangeFn get_addr_range_fn() {
       fn = reinterpret_cast<AddrRangeFn>(p);
   });
   return fn;
+}
+
+int check_peer_shape(const char* what, int64_t rows, int64_t D, int dtype, int world) {
+  if (world < 1 || world > kMaxPeers)
+    return kf::set_error(KF_ERR_INVALID, "%s: need 1 <= world <= %d", what, kMaxPeers);
+  if (rows <= 0 || rows > 0x7fffffffLL || D < 8 || D > 128 || D % 8)
+    return kf::set_error(KF_ERR_INVALID, "%s: need rows > 0 and D a multiple of 8 in [8, 128]", what);
+  if (dtype != KF_F16 && dtype != KF_BF16)
+    return kf::set_error(KF_ERR_INVALID, "%s: dtype must be fp16 or bf16", what);
+  return KF_OK;
+}
+
+bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
+int peer_set(const char* what, void* const* mailboxes, int world, int rank, PeerSet& peers) {
+  if (!mailboxes) return kf::set_error(KF_ERR_INVALID, "%s: null mailboxes", what);
+  if (rank < 0 || rank >= world) return kf::set_error(KF_ERR_INVALID, "%s: need 0 <= rank < world", what);
+  peers = PeerSet{};
+  for (int r = 0; r < world; ++r) {
+    peers.mailbox[r] = static_cast<uint8_t*>(mailboxes[r]);
+    if (!peers.mailbox[r] || misaligned(peers.mailbox[r], 256))
+      return kf::set_error(KF_ERR_INVALID, "%s: mailboxes must be 256-byte aligned", what);
+  }
+  return KF_OK;
+}
+
+size_t merge_smem(int S, int D) {
+  const int groups = kMergeThreads / (D / 4);
+  return (size_t)(((S + 3) & ~3) + groups * D) * sizeof(float);
+}
+
+template <bool BF16>
+int launch_peer_merge(const MergeArgs& m, uint8_t* mailbox, int world, int32_t* status, cudaStream_t st,
+                      const char* what) {
+  return launch_dependent(peer_merge_kernel<BF16>, dim3((unsigned)m.rows), dim3(kMergeThreads),
+                          merge_smem(world, m.D), st, what, m, mailbox, world, status);
 }
 
 }  // namespace
@@ -1519,55 +1640,35 @@ extern "C" int kf_ipc_close_handle(void* ptr, uint64_t offset) {
   return KF_OK;
 }
 
-namespace {
-
-int check_peer_shape(const char* what, int64_t rows, int64_t D, int dtype, int world) {
-  if (world < 1 || world > kMaxPeers)
-    return kf::set_error(KF_ERR_INVALID, "%s: need 1 <= world <= %d", what, kMaxPeers);
-  if (rows <= 0 || rows > 0x7fffffffLL || D < 8 || D > 128 || D % 8)
-    return kf::set_error(KF_ERR_INVALID, "%s: need rows > 0 and D a multiple of 8 in [8, 128]", what);
-  if (dtype != KF_F16 && dtype != KF_BF16)
-    return kf::set_error(KF_ERR_INVALID, "%s: dtype must be fp16 or bf16", what);
-  return KF_OK;
-}
-
-bool misaligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
-
-}  // namespace
-
 extern "C" int kf_decode_peer_put(const void* o, const float* lse, int64_t rows, int64_t D, int dtype,
                                   void* const* mailboxes, int world, int rank, void* stream) {
-  using kf::set_error;
-  if (!o || !lse || !mailboxes) return set_error(KF_ERR_INVALID, "kf_decode_peer_put: null argument");
-  int rc = check_peer_shape("kf_decode_peer_put", rows, D, dtype, world);
+  const char* what = "kf_decode_peer_put";
+  if (!o || !lse) return kf::set_error(KF_ERR_INVALID, "%s: null argument", what);
+  int rc = check_peer_shape(what, rows, D, dtype, world);
   if (rc) return rc;
-  if (rank < 0 || rank >= world) return set_error(KF_ERR_INVALID, "kf_decode_peer_put: need 0 <= rank < world");
-  if (misaligned(o, 16) || misaligned(lse, 4)) return set_error(KF_ERR_INVALID, "kf_decode_peer_put: misaligned buffers");
-  PeerSet peers = {};
-  for (int r = 0; r < world; ++r) {
-    peers.mailbox[r] = static_cast<uint8_t*>(mailboxes[r]);
-    if (!peers.mailbox[r] || misaligned(peers.mailbox[r], 256))
-      return set_error(KF_ERR_INVALID, "kf_decode_peer_put: mailboxes must be 256-byte aligned");
-  }
+  PeerSet peers;
+  if ((rc = peer_set(what, mailboxes, world, rank, peers))) return rc;
+  if (misaligned(o, 16) || misaligned(lse, 4)) return kf::set_error(KF_ERR_INVALID, "%s: misaligned buffers", what);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 grid(peer_layout(world, rows, (int)D).chunks, world);
+  const int64_t rpp = put_rows_per_piece(rows, (int)D);
+  const dim3 grid((unsigned)((rows + rpp - 1) / rpp), world);
   if (dtype == KF_BF16)
-    peer_put_kernel<true><<<grid, kPeerThreads, 0, st>>>(static_cast<const uint16_t*>(o), lse, rows, (int)D, peers,
-                                                         world, rank);
+    peer_put_kernel<true><<<grid, kPeerThreads, 0, st>>>(static_cast<const uint16_t*>(o), lse, rows, (int)D, rpp,
+                                                         peers, world, rank);
   else
-    peer_put_kernel<false><<<grid, kPeerThreads, 0, st>>>(static_cast<const uint16_t*>(o), lse, rows, (int)D, peers,
-                                                          world, rank);
-  return kf::check_launch("kf_decode_peer_put");
+    peer_put_kernel<false><<<grid, kPeerThreads, 0, st>>>(static_cast<const uint16_t*>(o), lse, rows, (int)D, rpp,
+                                                          peers, world, rank);
+  return kf::check_launch(what);
 }
 
 extern "C" int kf_decode_peer_merge(void* mailbox, int64_t rows, int64_t D, int dtype, int world, void* out,
                                     float* out_lse, int32_t* status, void* stream) {
-  using kf::set_error;
-  if (!mailbox || !out) return set_error(KF_ERR_INVALID, "kf_decode_peer_merge: null argument");
-  int rc = check_peer_shape("kf_decode_peer_merge", rows, D, dtype, world);
+  const char* what = "kf_decode_peer_merge";
+  if (!mailbox || !out) return kf::set_error(KF_ERR_INVALID, "%s: null argument", what);
+  int rc = check_peer_shape(what, rows, D, dtype, world);
   if (rc) return rc;
   if (misaligned(mailbox, 256) || misaligned(out, 8) || misaligned(out_lse, 4))
-    return set_error(KF_ERR_INVALID, "kf_decode_peer_merge: misaligned buffers");
+    return kf::set_error(KF_ERR_INVALID, "%s: misaligned buffers", what);
   MergeArgs m = {};
   m.rows = rows;
   m.D = (int)D;
@@ -1577,15 +1678,10 @@ extern "C" int kf_decode_peer_merge(void* mailbox, int64_t rows, int64_t D, int 
   m.Sq = 1;
   m.os0 = D;
   m.S = world;
-  const int groups = kMergeThreads / ((int)D / 4);
-  const size_t smem = (size_t)(((world + 3) & ~3) + groups * D) * sizeof(float);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* mb = static_cast<uint8_t*>(mailbox);
-  if (dtype == KF_BF16)
-    return launch_dependent(peer_merge_kernel<true>, dim3((unsigned)rows), dim3(kMergeThreads), smem, st,
-                            "kf_decode_peer_merge", m, mb, world, status);
-  return launch_dependent(peer_merge_kernel<false>, dim3((unsigned)rows), dim3(kMergeThreads), smem, st,
-                          "kf_decode_peer_merge", m, mb, world, status);
+  return dtype == KF_BF16 ? launch_peer_merge<true>(m, mb, world, status, st, what)
+                          : launch_peer_merge<false>(m, mb, world, status, st, what);
 }
 
 extern "C" int kf_decode_peer_exchange(const void* o, const float* lse, int64_t rows, int64_t D,
@@ -1597,4 +1693,60 @@ extern "C" int kf_decode_peer_exchange(const void* o, const float* lse, int64_t 
   int rc = kf_decode_peer_put(o, lse, rows, D, dtype, mailboxes, world, rank, stream);
   if (rc) return rc;
   return kf_decode_peer_merge(mailboxes[rank], rows, D, dtype, world, out, out_lse, status, stream);
+}
+
+namespace {
+
+// Split kernel + merge_put (the send half of kf_decode_kv_split_peer); fills `local`.
+int kv_split_send(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const kf_tensor4* o, float* lse,
+                  int dtype, float scale, int num_splits, void* workspace, size_t workspace_bytes,
+                  void* const* mailboxes, int world, int rank, cudaStream_t st, const char* what, PeerSet& peers,
+                  MergeArgs& local) {
+  if (num_splits < 1) return kf::set_error(KF_ERR_INVALID, "%s: num_splits must be >= 1", what);
+  DecodeArgs a;
+  int rc = decode_setup(q, k, v, nullptr, nullptr, 0, o, lse, dtype, scale, num_splits, workspace,
+                        workspace_bytes, true, what, a);
+  if (rc != KF_OK) return rc;
+  if ((rc = check_peer_shape(what, a.prow_total, a.D, dtype, world))) return rc;
+  if ((rc = peer_set(what, mailboxes, world, rank, peers))) return rc;
+  if (a.num_splits > 2 * kMergeThreads)
+    return kf::set_error(KF_ERR_UNSUPPORTED, "%s: at most %d splits", what, 2 * kMergeThreads);
+  rc = dtype == KF_BF16 ? dispatch_split<true>(a, k, v, st) : dispatch_split<false>(a, k, v, st);
+  if (rc != KF_OK) return rc;
+  local = merge_args_of(a);
+  const size_t smem = merge_smem(local.S, local.D);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(merge_put_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kf::set_error(KF_ERR_CUDA, "%s: cannot reserve %zu bytes of shared memory", what, smem);
+  return launch_dependent(merge_put_kernel, dim3((unsigned)local.rows), dim3(kMergeThreads), smem, st, what, local,
+                          peers, world, rank);
+}
+
+}  // namespace
+
+extern "C" int kf_decode_kv_split_peer_send(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                                            int dtype, float scale, int num_splits, void* workspace,
+                                            size_t workspace_bytes, void* const* mailboxes, int world, int rank,
+                                            void* stream) {
+  PeerSet peers;
+  MergeArgs local;
+  // no output here: q stands in for O's descriptor (shape checks only)
+  return kv_split_send(q, k, v, q, nullptr, dtype, scale, num_splits, workspace, workspace_bytes, mailboxes, world,
+                       rank, static_cast<cudaStream_t>(stream), "kf_decode_kv_split_peer_send", peers, local);
+}
+
+extern "C" int kf_decode_kv_split_peer(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
+                                       const kf_tensor4* o, float* lse, int dtype, float scale, int num_splits,
+                                       void* workspace, size_t workspace_bytes, void* const* mailboxes,
+                                       int world, int rank, int32_t* status, void* stream) {
+  const char* what = "kf_decode_kv_split_peer";
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  PeerSet peers;
+  MergeArgs m;
+  int rc = kv_split_send(q, k, v, o, lse, dtype, scale, num_splits, workspace, workspace_bytes, mailboxes, world,
+                         rank, st, what, peers, m);
+  if (rc != KF_OK) return rc;
+  m.S = world;  // the final merge writes O/LSE with the caller's strides
+  return dtype == KF_BF16 ? launch_peer_merge<true>(m, peers.mailbox[rank], world, status, st, what)
+                          : launch_peer_merge<false>(m, peers.mailbox[rank], world, status, st, what);
 }

@@ -15,9 +15,9 @@ allows:
   ``[B, Hq, Sq, D + 1]`` (fp32), and every rank merges them with the
   LSE-weighted merge kernel (the same math as the reference's split-KV
   reduce, triton_forward.py:287-349).  ``PeerExchange`` replaces the
-  all-gather + merge by two kernels over NVLink peer memory: each rank stores
-  its partial straight into every peer's mailbox and merges what arrives in
-  its own.
+  all-gather + merge over NVLink peer memory: the kernel that merges a
+  rank's own splits stores the fp32 result straight into every peer's
+  mailbox, and one more kernel merges what arrives in the rank's own.
 """
 from __future__ import annotations
 
@@ -28,7 +28,7 @@ import torch
 import torch.distributed as dist
 
 from . import _ext
-from ._planning import cdiv
+from ._planning import cdiv, split_kv_plan
 
 
 def shard_units(batch: int, kv_heads: int, world: int, rank: int) -> List[Tuple[int, int]]:
@@ -154,6 +154,30 @@ class PeerExchange:
         if self.world > 1:
             dist.barrier(group=group)  # every rank mapped every mailbox
 
+    def decode(self, q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, *,
+               scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Split-KV decode of this rank's key chunk fused with the exchange
+        (``kf_decode_kv_split_peer``): the split kernel, one kernel that
+        merges this rank's splits and stores the fp32 result into every
+        mailbox, and the final merge.  Returns the full (O, LSE)."""
+        b, hq, sq, d = q.shape
+        if q.dtype != self.dtype or d != self.d or b * hq * sq != self.rows:
+            raise ValueError("PeerExchange.decode: q does not match the exchange's rows/d/dtype")
+        hkv, sk = k_local.shape[1], k_local.shape[2]
+        plan = split_kv_plan(sq, sk, d, causal=False, batch=b, q_heads=hq, kv_heads=hkv,
+                             sm_count=_ext.sm_count(self.device.index))
+        ws = self.lib.kf_decode_workspace_bytes(b, hq, sq, d, max(2, plan.num_splits))
+        workspace = torch.empty(ws, dtype=torch.uint8, device=q.device)
+        out = torch.empty((b, hq, sq, d), dtype=q.dtype, device=q.device)
+        lse = torch.empty((b, hq, sq), dtype=torch.float32, device=q.device)
+        rc = self.lib.kf_decode_kv_split_peer(
+            _ext.ref(_ext.t4(q)), _ext.ref(_ext.t4(k_local)), _ext.ref(_ext.t4(v_local)),
+            _ext.ref(_ext.t4(out)), lse.data_ptr(), self.dtype_code, float(scale), int(plan.num_splits),
+            workspace.data_ptr(), int(workspace.numel()), self.ptrs, self.world, self.rank,
+            self.status_word.data_ptr(), _ext.stream_of(q))
+        _ext.check(rc, "kf_decode_kv_split_peer")
+        return out, lse
+
     def exchange(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor = None,
                  out_lse: torch.Tensor = None) -> Tuple[torch.Tensor, torch.Tensor]:
         if o.dtype != self.dtype or o.shape[-1] != self.d or o[..., 0].numel() != self.rows:
@@ -197,8 +221,8 @@ def decode_kv_split(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tenso
     """
     from .attention import _decode_forward
 
-    o, lse = _decode_forward(q, k_local, v_local, scale=scale, want_lse=True)
     if exchange is not None:
-        return exchange.exchange(o, lse)
+        return exchange.decode(q, k_local, v_local, scale=scale)
+    o, lse = _decode_forward(q, k_local, v_local, scale=scale, want_lse=True)
     part_o, part_lse = gather_partials(pack_partial(o, lse), group)
     return merge_partials(part_o, part_lse, tuple(q.shape), q.dtype)

@@ -1,11 +1,11 @@
 # SPDX-License-Identifier: Apache-2.0
 """Peer-memory exchange of decode partials (kf_decode_peer_put / _merge /
-_exchange) vs the fp32 oracle merge.
+_exchange, and the fused kf_decode_kv_split_peer[_send]) vs the fp32 oracle.
 
-On one GPU, W ranks are emulated by W mailboxes in this process: all puts are
-launched first, then the merges, so every wait is on a flag that an earlier,
-already finished kernel set.  The 2-GPU test runs real ranks (one process per
-GPU, NVLS off) and skips when fewer GPUs are visible."""
+On one GPU, W ranks are emulated by W mailboxes in this process: all sends
+are launched first, then the merges, so every wait is on a counter that
+earlier, already finished kernels filled.  The 2-GPU test runs real ranks
+(one process per GPU, NVLS off) and skips when fewer GPUs are visible."""
 import ctypes
 import datetime
 import os
@@ -87,17 +87,24 @@ def test_emulated_ranks_merge_matches_oracle(world, rows, d, dtype):
             torch.testing.assert_close(out_lses[r], el.to(out_lses[r].device), rtol=1e-5, atol=1e-5)
 
 
-def test_emulated_kv_split_decode_matches_full_decode():
-    # cfg3 shapes (B2 Hq8 Hkv2 D64 fp16), Sq=4, the KV sequence split over 4 emulated ranks
-    world, sk = 4, 5000
-    q = _rand((2, 8, 4, 64), torch.float16, 1)
-    k = _rand((2, 2, sk, 64), torch.float16, 2)
-    v = _rand((2, 2, sk, 64), torch.float16, 3)
-    parts, lses = [], []
+def _kv_split_inputs(world, sk, sq=4, dtype=torch.float16):
+    # cfg3 shapes (B2 Hq8 Hkv2 D64), the KV sequence split over `world` ranks
+    q = _rand((2, 8, sq, 64), dtype, 1)
+    k = _rand((2, 2, sk, 64), dtype, 2)
+    v = _rand((2, 2, sk, 64), dtype, 3)
+    chunks = []
     for r in range(world):
         lo, hi = kd.kv_chunk(sk, world, r)
-        o, lse = _decode_forward(q, k[:, :, lo:hi].contiguous(), v[:, :, lo:hi].contiguous(),
-                                 scale=0.125, want_lse=True)
+        chunks.append((k[:, :, lo:hi].contiguous(), v[:, :, lo:hi].contiguous()))
+    return q, k, v, chunks
+
+
+def test_emulated_kv_split_decode_via_put_matches_full_decode():
+    world, sk = 4, 5000
+    q, k, v, chunks = _kv_split_inputs(world, sk)
+    parts, lses = [], []
+    for kl, vl in chunks:
+        o, lse = _decode_forward(q, kl, vl, scale=0.125, want_lse=True)
         parts.append(o)
         lses.append(lse)
     rows = 2 * 8 * 4
@@ -112,6 +119,46 @@ def test_emulated_kv_split_decode_matches_full_decode():
     for r in range(world):
         check_close(outs[r], eo, name=f"kv-split decode rank{r}")
         check_close(out_lses[r], el, name=f"kv-split lse rank{r}")
+
+
+@pytest.mark.parametrize("world,sk,sq,dtype", [
+    (2, 131072, 1, torch.float16),   # cfg3 long context
+    (4, 5000, 4, torch.bfloat16),
+    (8, 20000, 16, torch.float16),   # tensor-core decode kernel per rank
+    (3, 700, 2, torch.bfloat16),     # one split per rank (partials forced)
+])
+def test_emulated_fused_kv_split_send_matches_full_decode(world, sk, sq, dtype):
+    from kotflash_b200._planning import split_kv_plan
+
+    lib = _ext.load()
+    q, k, v, chunks = _kv_split_inputs(world, sk, sq, dtype)
+    rows = 2 * 8 * sq
+    mb = _Mailboxes(world, rows, 64)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    code = _ext.dtype_code(dtype)
+    eo, el = oracle.forward(q, k, v, causal=False, scale=0.125)
+    for epoch in range(2):
+        keep = []
+        for r, (kl, vl) in enumerate(chunks):
+            plan = split_kv_plan(sq, kl.shape[2], 64, causal=False, batch=2, q_heads=8, kv_heads=2,
+                                 sm_count=_ext.sm_count(0))
+            ws = torch.empty(lib.kf_decode_workspace_bytes(2, 8, sq, 64, max(2, plan.num_splits)),
+                             dtype=torch.uint8, device="cuda")
+            keep.append(ws)
+            _ext.check(lib.kf_decode_kv_split_peer_send(
+                _ext.ref(_ext.t4(q)), _ext.ref(_ext.t4(kl)), _ext.ref(_ext.t4(vl)), code, 0.125,
+                int(plan.num_splits), ws.data_ptr(), int(ws.numel()), mb.ptrs, world, r, stream), "send")
+        outs = [torch.empty(rows, 64, dtype=dtype, device="cuda") for _ in range(world)]
+        out_lses = [torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(world)]
+        for r in range(world):
+            _ext.check(lib.kf_decode_peer_merge(mb.ptrs[r], rows, 64, code, world, outs[r].data_ptr(),
+                                                out_lses[r].data_ptr(), status.data_ptr(), stream), "merge")
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        for r in range(world):
+            check_close(outs[r].reshape(q.shape), eo, name=f"fused send W{world} Sq{sq} rank{r} epoch{epoch}")
+            check_close(out_lses[r].reshape(q.shape[:-1]), el, name=f"fused send lse rank{r}")
 
 
 def test_emulated_exchange_replays_in_a_cuda_graph():
@@ -178,6 +225,19 @@ def test_one_rank_peer_exchange_is_identity():
         torch.cuda.synchronize()
         torch.testing.assert_close(out, o, rtol=0, atol=0)
         torch.testing.assert_close(out_lse, lse, rtol=1e-6, atol=1e-6)
+    assert ex.status() == 0
+    ex.close()
+
+
+def test_one_rank_fused_decode_matches_single_gpu_decode():
+    q, k, v, _ = _kv_split_inputs(1, 3000, 16, torch.bfloat16)
+    ex = kd.PeerExchange(rows=2 * 8 * 16, d=64, dtype=torch.bfloat16)
+    for _ in range(3):
+        o, lse = kd.decode_kv_split(q, k, v, scale=0.125, exchange=ex)
+        ro, rl = _decode_forward(q, k, v, scale=0.125, want_lse=True)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(o, ro, rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(lse, rl, rtol=1e-5, atol=1e-5)
     assert ex.status() == 0
     ex.close()
 
