@@ -1372,7 +1372,8 @@ extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const
 // holds W * rows * ((e + 1) / 2) modulo 2^32, and no intermediate value of
 // an epoch equals it.
 //
-// Mailbox layout: [0, 256) control words {completed epochs, done ticket},
+// Mailbox layout: [0, 256) control words {completed epochs, merge ticket,
+// send ticket},
 // then two halves of {O [W][rows][D] fp32, LSE [W][rows] fp32, counter}.
 namespace {
 
@@ -1475,10 +1476,19 @@ __global__ void __launch_bounds__(kMergeThreads) merge_put_kernel(const MergeArg
       if (c4 == 0) h.lse[slot] = l;
     }
   });
+  // One signal per grid: every CTA orders its stores before its ticket
+  // (gpu-scope fence); the CTA that takes the last ticket then releases all
+  // rows at system scope, one counter add per receiver.
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < world; ++p) red_release_sys_add(peer_half(peers.mailbox[p], L, e).counter, 1u);
+    uint32_t* ticket = reinterpret_cast<uint32_t*>(peers.mailbox[rank]) + 2;
+    __threadfence();
+    if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
+      *ticket = 0;
+      __threadfence_system();
+      for (int p = 0; p < world; ++p)
+        red_release_sys_add(peer_half(peers.mailbox[p], L, e).counter, (uint32_t)a.rows);
+    }
   }
 }
 
