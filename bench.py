@@ -376,6 +376,20 @@ def bench_cache_loop(peaks):
     ms_app = _graph_time(lambda i: _append_at(cache, pk, pv, 0), 8)
     app_bytes = 2 * 2 * pk.numel() * 2  # read new K,V + write cache K,V
     cache.append(pk, pv)
+    # prefill attention reading the cache's strided prefix view in place (K1), the
+    # reference example's prefill -> decode handoff (examples/gqa_kv_cache_decode.py:58-65)
+    from kotflash_b200 import attention
+
+    q_pre = (torch.randn(b, hq, pre, d, device="cuda", generator=g) * d ** -0.5).bfloat16()
+
+    def prefill(_i):
+        with torch.inference_mode():
+            ck, cv = cache.view()
+            attention(q_pre, ck, cv, causal=True, backend="triton")
+
+    ms_pre = _graph_time(prefill, 3, replays=3)
+    f_pre = fwd_flops(b, hq, pre, pre, d, True)
+    del q_pre
     nk = torch.randn(steps, b, hkv, 1, d, device="cuda", generator=g).bfloat16()
     nv = torch.randn(steps, b, hkv, 1, d, device="cuda", generator=g).bfloat16()
     qq = torch.randn(steps, b, hq, 1, d, device="cuda", generator=g).bfloat16()
@@ -395,6 +409,10 @@ def bench_cache_loop(peaks):
         "prefill_append": {"tokens": pre, "us": round(ms_app * 1e3, 2),
                            "hbm_gbs": round(app_bytes / (ms_app * 1e-3) / 1e9, 1),
                            "hbm_frac": round(app_bytes / (ms_app * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)},
+        "prefill_attention": {"tokens": pre, "ms": round(ms_pre, 4),
+                              "tflops": round(f_pre / ms_pre / 1e9, 1),
+                              "frac": round(f_pre / ms_pre / 1e9 / peaks["bf16_tflops"], 3),
+                              "note": "causal K1 forward over the strided cache view (capacity 32768), no copy"},
         "steps": steps, "us_per_step": round(ms * 1e3, 2), "us_per_token": round(ms * 1e3, 2),
         "loop_ms": round(ms * steps, 3), "hbm_gbs": round(gbs, 1),
         "hbm_frac": round(gbs / peaks["hbm_gbs"], 3),
@@ -495,6 +513,85 @@ def bench_decode_multi_gpu(world, rank):
                              "us_per_token": round(n * 1e3 / sq, 3)},
                     "timing": "CUDA-graph replay, max over ranks"})
         torch.cuda.synchronize()
+    return out
+
+
+# --------------------------------------------------------------------------- GPU comparator
+def bench_sdpa_comparators(dtype):
+    """PyTorch SDPA's own GPU backends (cuDNN, flash, memory-efficient) on this
+    B200 at the prefill config (fwd+bwd, causal, GQA through ``enable_gqa``)
+    and at the cfg3 decode point (Sq=1, Sk=131072): a reference point beside
+    the roofline, since the reference's own Triton route cannot run on sm_100.
+    CUDA events, warm-up first; a backend that rejects the inputs is reported
+    with its error."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    backends = {"cudnn": SDPBackend.CUDNN_ATTENTION, "flash": SDPBackend.FLASH_ATTENTION,
+                "efficient": SDPBackend.EFFICIENT_ATTENTION}
+    b, hq, s, d = CFG["B"], CFG["Hq"], CFG["S"], CFG["D"]
+    f_fwd = fwd_flops(b, hq, s, s, d, True)
+    out = {"prefill": {}, "decode_sq1_sk131072": {}}
+    q, k, v, do = make_prefill_inputs(dtype, 4321, "cuda")
+    for name, be in backends.items():
+        try:
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+
+            def step():
+                with sdpa_kernel([be]):
+                    o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=True)
+                return o, torch.autograd.grad(o, (qq, kk, vv), do)
+
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(5)]
+            for e in evs:
+                e[0].record()
+                with sdpa_kernel([be]):
+                    o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=True)
+                e[1].record()
+                torch.autograd.grad(o, (qq, kk, vv), do)
+                e[2].record()
+            torch.cuda.synchronize()
+            fwd = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
+            tot = statistics.median(e[0].elapsed_time(e[2]) for e in evs)
+            out["prefill"][name] = {"fwd_ms": round(fwd, 4), "fwd_bwd_ms": round(tot, 4),
+                                    "fwd_tflops": round(f_fwd / fwd / 1e9, 1),
+                                    "fwd_bwd_tflops": round(3.5 * f_fwd / tot / 1e9, 1)}
+        except Exception as exc:  # backend not available for these inputs
+            out["prefill"][name] = {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}"}
+        torch.cuda.empty_cache()
+    del q, k, v, do
+    sk, copies = 131072, 2
+    g = torch.Generator(device="cuda").manual_seed(77)
+    ks = torch.randn(copies, 2, 2, sk, 64, device="cuda", generator=g).half()
+    vs = torch.randn(copies, 2, 2, sk, 64, device="cuda", generator=g).half()
+    qs = torch.randn(copies, 2, 8, 1, 64, device="cuda", generator=g).half()
+    alg = 1024 * sk + 4096 + 64
+    for name, be in backends.items():
+        try:
+            def call(i):
+                with sdpa_kernel([be]):
+                    F.scaled_dot_product_attention(qs[i % copies], ks[i % copies], vs[i % copies], enable_gqa=True)
+
+            for i in range(3):
+                call(i)
+            torch.cuda.synchronize()
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for i in range(20):
+                call(i)
+            e.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(e) / 20
+            out["decode_sq1_sk131072"][name] = {"us_per_call": round(ms * 1e3, 2),
+                                                "hbm_gbs": round(alg / (ms * 1e-3) / 1e9, 1),
+                                                "timing": "eager launches, 2 rotating K/V sets (268 MB)"}
+        except Exception as exc:
+            out["decode_sq1_sk131072"][name] = {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}"}
+    del ks, vs, qs
+    torch.cuda.empty_cache()
     return out
 
 
@@ -632,6 +729,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-comparators", action="store_true",
+                    help="skip timing PyTorch SDPA's own GPU backends")
     ap.add_argument("--decode-case", default=None, metavar="SQ,SK",
                     help="time only the split-KV decode config (B2 Hq8 Hkv2 D64 fp16) at one "
                          "(Sq, Sk) with --warmup/--steps plain launches; prints one JSON line")
@@ -692,6 +791,8 @@ def main(argv=None) -> int:
         elif rank == 0:
             decode = {"sweep": bench_decode_sweep(peaks), "kv_cache_loop": bench_cache_loop(peaks)}
     odd = bench_odd_head_dim(peaks) if (rank == 0 and world == 1 and not args.no_decode) else None
+    comparators = (bench_sdpa_comparators(dtype)
+                   if (rank == 0 and world == 1 and not args.no_comparators) else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -718,6 +819,7 @@ def main(argv=None) -> int:
             "cpu_baseline": cpu,
             "decode": decode, "decode_multi_gpu": multi,
             "odd_head_dim_training": odd,
+            "gpu_comparators": comparators,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
