@@ -516,6 +516,99 @@ def bench_decode_multi_gpu(world, rank):
     return out
 
 
+# --------------------------------------------------------------------------- decoder block
+class DecoderBlock(torch.nn.Module):
+    """Pre-norm GQA decoder block (LayerNorm, Q/K/V/O projections, SiLU-gated
+    MLP of width 4x) with fp32 parameters whose attention runs in 16-bit: the
+    block of the reference's decoder-block benchmark
+    (benchmarks/benchmark_decoder_block.py:34-103), kept structurally alike so
+    the step times compare."""
+
+    def __init__(self, q_heads, kv_heads, head_dim, mlp_ratio=4):
+        super().__init__()
+        nn = torch.nn
+        hidden = q_heads * head_dim
+        self.hq, self.hkv, self.d = q_heads, kv_heads, head_dim
+        self.norm1, self.norm2 = nn.LayerNorm(hidden), nn.LayerNorm(hidden)
+        self.wq = nn.Linear(hidden, hidden, bias=False)
+        self.wk = nn.Linear(hidden, kv_heads * head_dim, bias=False)
+        self.wv = nn.Linear(hidden, kv_heads * head_dim, bias=False)
+        self.wo = nn.Linear(hidden, hidden, bias=False)
+        self.w_gate = nn.Linear(hidden, mlp_ratio * hidden, bias=False)
+        self.w_up = nn.Linear(hidden, mlp_ratio * hidden, bias=False)
+        self.w_down = nn.Linear(mlp_ratio * hidden, hidden, bias=False)
+
+    def forward(self, x, backend, attn_dtype=torch.float16):
+        import torch.nn.functional as F
+        from kotflash_b200 import attention
+
+        b, s, h = x.shape
+        y = self.norm1(x)
+        q = self.wq(y).view(b, s, self.hq, self.d).transpose(1, 2).to(attn_dtype)
+        k = self.wk(y).view(b, s, self.hkv, self.d).transpose(1, 2).to(attn_dtype)
+        v = self.wv(y).view(b, s, self.hkv, self.d).transpose(1, 2).to(attn_dtype)
+        if backend == "kotflash_b200":
+            a = attention(q, k, v, causal=True, backend="triton")
+        elif backend == "sdpa_gqa":
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        else:  # "sdpa_expanded_kv"
+            g = self.hq // self.hkv
+            a = F.scaled_dot_product_attention(q, k.repeat_interleave(g, 1), v.repeat_interleave(g, 1),
+                                               is_causal=True)
+        x = x + self.wo(a.transpose(1, 2).reshape(b, s, h).to(x.dtype))
+        y = self.norm2(x)
+        return x + self.w_down(F.silu(self.w_gate(y)) * self.w_up(y))
+
+
+def decoder_block_step(model, opt, x, target, backend):
+    import torch.nn.functional as F
+
+    opt.zero_grad(set_to_none=True)
+    loss = F.mse_loss(model(x, backend), target)
+    loss.backward()
+    opt.step()
+    return loss.detach()
+
+
+def bench_decoder_block(batch=2, seq=4096, q_heads=32, kv_heads=8, head_dim=128, warmup=3, iters=5):
+    """Training step (forward, backward, AdamW) of the decoder block per
+    attention backend, same initial weights and inputs; tokens/s from the
+    median CUDA-event step time.  fp32 projections (no TF32), fp16 attention,
+    as the reference benchmark runs it."""
+    torch.manual_seed(1234)
+    hidden = q_heads * head_dim
+    x = torch.randn(batch, seq, hidden, device="cuda")
+    target = torch.randn_like(x)
+    init = {k: v.detach().clone() for k, v in DecoderBlock(q_heads, kv_heads, head_dim).state_dict().items()}
+    out = {"shape": {"batch": batch, "seq": seq, "q_heads": q_heads, "kv_heads": kv_heads, "head_dim": head_dim,
+                     "hidden": hidden},
+           "precision": "fp32 parameters and projections (TF32 off), fp16 attention, AdamW"}
+    for backend in ("kotflash_b200", "sdpa_gqa", "sdpa_expanded_kv"):
+        try:
+            model = DecoderBlock(q_heads, kv_heads, head_dim).cuda()
+            model.load_state_dict(init)
+            opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
+            for _ in range(warmup):
+                decoder_block_step(model, opt, x, target, backend)
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+            loss = None
+            for a, e in evs:
+                a.record()
+                loss = decoder_block_step(model, opt, x, target, backend)
+                e.record()
+            torch.cuda.synchronize()
+            ms = statistics.median(a.elapsed_time(e) for a, e in evs)
+            out[backend] = {"step_ms": round(ms, 3), "tokens_per_s": round(batch * seq * 1e3 / ms, 1),
+                            "last_loss": round(float(loss), 6),
+                            "params_finite": all(bool(torch.isfinite(p).all()) for p in model.parameters())}
+            del model, opt
+        except Exception as exc:
+            out[backend] = {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}"}
+        torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------- GPU comparator
 def bench_sdpa_comparators(dtype):
     """PyTorch SDPA's own GPU backends (cuDNN, flash, memory-efficient) on this
@@ -793,6 +886,7 @@ def main(argv=None) -> int:
     odd = bench_odd_head_dim(peaks) if (rank == 0 and world == 1 and not args.no_decode) else None
     comparators = (bench_sdpa_comparators(dtype)
                    if (rank == 0 and world == 1 and not args.no_comparators) else None)
+    block = bench_decoder_block() if (rank == 0 and world == 1 and not args.no_comparators) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -820,6 +914,7 @@ def main(argv=None) -> int:
             "decode": decode, "decode_multi_gpu": multi,
             "odd_head_dim_training": odd,
             "gpu_comparators": comparators,
+            "decoder_block_training_step": block,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
