@@ -140,19 +140,28 @@ class PeerExchange:
             allh = [mine]
         self._opened = []
         ptrs = []
+        error = ""
         for r, (h, off) in enumerate(allh):
             if r == self.rank:
                 ptrs.append(self.local)
                 continue
             hb = (ctypes.c_uint8 * self.HANDLE_BYTES).from_buffer_copy(h)
             p = ctypes.c_void_p()
-            _ext.check(self.lib.kf_ipc_open_handle(hb, ctypes.c_uint64(off), ctypes.byref(p)),
-                       "kf_ipc_open_handle")
+            if self.lib.kf_ipc_open_handle(hb, ctypes.c_uint64(off), ctypes.byref(p)) != _ext.KF_OK:
+                error = f"rank {self.rank} cannot map rank {r}'s mailbox: {_ext.last_error()}"
+                break
             self._opened.append((p.value, off))
             ptrs.append(p.value)
-        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         if self.world > 1:
-            dist.barrier(group=group)  # every rank mapped every mailbox
+            # every rank learns whether all mappings succeeded (the same collective on all ranks)
+            ok = torch.tensor([0 if error else 1], dtype=torch.int32, device=self.device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if int(ok.item()) == 0:
+                self.close()
+                raise RuntimeError("PeerExchange: " + (error or "a peer could not map the mailboxes"))
+        elif error:
+            raise RuntimeError("PeerExchange: " + error)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
 
     def decode(self, q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor, *,
                scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
