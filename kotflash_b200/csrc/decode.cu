@@ -1423,6 +1423,9 @@ KF_DEVI uint32_t current_epoch(const uint8_t* mailbox) {
 KF_DEVI void red_release_sys_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+KF_DEVI void red_relaxed_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 KF_DEVI uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -1477,17 +1480,24 @@ __global__ void __launch_bounds__(kMergeThreads) merge_put_kernel(const MergeArg
     }
   });
   // One signal per grid: every CTA orders its stores before its ticket
-  // (gpu-scope fence); the CTA that takes the last ticket then releases all
-  // rows at system scope, one counter add per receiver.
+  // (gpu-scope fence); in the CTA that takes the last ticket, lane p of warp 0
+  // releases all rows to receiver p: a system-scope fence, then a relaxed add
+  // to p's arrival counter (fence + relaxed write is a release pattern).  The
+  // receivers' fences run in parallel instead of one release per receiver in
+  // turn, which grew the exchange with the rank count.
   __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t* ticket = reinterpret_cast<uint32_t*>(peers.mailbox[rank]) + 2;
-    __threadfence();
-    if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
-      *ticket = 0;
+  if (threadIdx.x < 32) {
+    int last = 0;
+    if (threadIdx.x == 0) {
+      uint32_t* ticket = reinterpret_cast<uint32_t*>(peers.mailbox[rank]) + 2;
+      __threadfence();
+      last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+      if (last) *ticket = 0;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last && (int)threadIdx.x < world) {
       __threadfence_system();
-      for (int p = 0; p < world; ++p)
-        red_release_sys_add(peer_half(peers.mailbox[p], L, e).counter, (uint32_t)a.rows);
+      red_relaxed_sys_add(peer_half(peers.mailbox[threadIdx.x], L, e).counter, (uint32_t)a.rows);
     }
   }
 }
