@@ -291,12 +291,16 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
             if (!(ok = wait_bar(&bars->p_full[t], (jt + j) & 1, bars, p.status))) break;
             kf::tc_fence_after();
             issue_pv(gj, j == 0);
-            release(&bars->v_empty[s]);
+            // PV and the next QK^T go out back to back (a commit between them
+            // would leave the tensor pipe, which queues almost nothing, idle).
             if (more) {
               issue_qk(gj + 1);
               kf::umma_commit(&bars->s_full[t]);
+              release(&bars->v_empty[s]);
               if (j + 2 == nblk) release(&bars->q_empty);  // last QK^T of the item
               release(&bars->k_empty[s1]);
+            } else {
+              release(&bars->v_empty[s]);
             }
           }
           kf::umma_commit(&bars->o_final[t]);
