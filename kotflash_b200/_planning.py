@@ -20,7 +20,7 @@ INT32_MAX = 2**31 - 1
 # Decode kernel tiling (kotflash_b200/csrc/decode.cu): keys per pipeline tile
 # and the minimum number of keys a split should own.
 DECODE_BLOCK_N = 64
-DECODE_MIN_KEYS_PER_SPLIT = 256
+DECODE_MIN_KEYS_PER_SPLIT = 64  # one K/V tile: a split's latency, not its length, sets short calls
 DECODE_MAX_SQ = 16
 DECODE_MAX_SPLITS = 512
 DEFAULT_SM_COUNT = 148
