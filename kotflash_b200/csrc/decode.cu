@@ -520,17 +520,21 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
 // (one M = 128 tile covers up to 128 rows).
 // CTA = (split, batch, KV head, block of up to 128 packed rows); rows sit on
 // TMEM lanes (M = 128, unused lanes are zero rows whose warps skip the
-// softmax).  Per 128-key tile: S = Q K^T (SS), softmax by one thread per row
-// (lazy rescale, P written back over S as 16-bit), O += P V (TS).  Warps 0-3
-// softmax + Q load, warp 4 TMEM allocation + MMA issue, warp 5 TMA producer.
+// softmax).  Per 64-key tile: S = Q K^T (SS) into one of two S buffers,
+// softmax by one thread per row (lazy rescale, P written back over S as
+// 16-bit), O += P V (TS).  With two S buffers the next tile's S is computed
+// while the softmax works on this one (one buffer measured 58% of HBM at
+// Sq = 16, Sk = 131072; two: 65%).  Warps 0-3 softmax + Q load, warp 4 TMEM
+// allocation + MMA issue, warp 5 TMA producer.  TMEM: S0 [0, 64), S1
+// [64, 128), O [128, 128 + D).
 constexpr int kTcThreads = 192;
-constexpr int kTcKeys = 128;
-constexpr int kTcStages = 2;
+constexpr int kTcKeys = 64;    // keys per K/V tile and per S buffer
+constexpr int kTcStages = 4;
 constexpr float kTcRescale = 8.0f;  // log2 units, as in the prefill forward
 
 struct __align__(8) TcBarriers {
   uint64_t full[kTcStages], empty[kTcStages];
-  uint64_t q_ready, s_full, p_full, o_done;
+  uint64_t q_ready, s_full[2], p_full[2], pv_done, o_done;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -556,8 +560,9 @@ template <bool BF16, int NP, int KS>
 __global__ void __launch_bounds__(kTcThreads, 2)
 decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                  const DecodeArgs a) {
-  constexpr int PANEL = kTcKeys * 128;   // 64 columns x 128 rows, 128-byte swizzle
+  constexpr int PANEL = kTcKeys * 128;   // K/V: 64 columns x kTcKeys rows, 128-byte swizzle
   constexpr int TILE = NP * PANEL;
+  constexpr int QPANEL = 128 * 128;      // Q: 64 columns x 128 rows
   constexpr int d_pad16 = KS * 16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -565,7 +570,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
   uint8_t* sK = smem;                          // [stage][NP][128 keys][64]
   uint8_t* sV = sK + kTcStages * TILE;
   uint8_t* sQ = sV + kTcStages * TILE;         // [NP][128 rows][64]
-  TcBarriers* bars = reinterpret_cast<TcBarriers*>(sQ + TILE);
+  TcBarriers* bars = reinterpret_cast<TcBarriers*>(sQ + NP * QPANEL);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x;
@@ -583,8 +588,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
       kf::mbar_init(&bars->empty[s], 1);
     }
     kf::mbar_init(&bars->q_ready, 128);
-    kf::mbar_init(&bars->s_full, 1);
-    kf::mbar_init(&bars->p_full, 32 * active_warps);
+    for (int i = 0; i < 2; ++i) {
+      kf::mbar_init(&bars->s_full[i], 1);
+      kf::mbar_init(&bars->p_full[i], 32 * active_warps);
+    }
+    kf::mbar_init(&bars->pv_done, 1);
     kf::mbar_init(&bars->o_done, 1);
     bars->abort_flag = 0;
     kf::fence_barrier_init();
@@ -635,25 +643,41 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
       const kf::SDesc dq = kf::make_sdesc_split(kf::smem_u32(sQ), 16, 1024);
       const kf::SDesc dk = kf::make_sdesc_split(kf::smem_u32(sK), 16, 1024);
       const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), PANEL, 1024);
-      bool ok = tc_wait(&bars->q_ready, 0, bars, a.status);
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int s = t % kTcStages;
-        if (!(ok = tc_wait(&bars->full[s], (t / kTcStages) & 1, bars, a.status))) break;
-        kf::tc_fence_after();
-        const uint32_t koff = s * TILE;
+      // S is double-buffered (S_t in columns 64 (t & 1)): S_{t+1} = Q K_{t+1}^T
+      // is issued before O += P_t V_t, so the softmax of tile t+1 can start
+      // as soon as it finishes tile t.  S_{t+1} overwrites P_{t-1}, which
+      // PV_{t-1} (issued earlier by this thread) has read.
+      auto issue_qk = [&](int t) {
+        const uint32_t koff = (t % kTcStages) * TILE;
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
-          kf::umma_ss(tmem, kf::sdesc_at(dq, off), kf::sdesc_at(dk, koff + off), idesc_qk, kk > 0);
+          const uint32_t qo = (kk >> 2) * QPANEL + (kk & 3) * 32, ko = (kk >> 2) * PANEL + (kk & 3) * 32;
+          kf::umma_ss(tmem + (t & 1) * kTcKeys, kf::sdesc_at(dq, qo), kf::sdesc_at(dk, koff + ko), idesc_qk,
+                      kk > 0);
         }
-        kf::umma_commit(&bars->s_full);
-        if (!(ok = tc_wait(&bars->p_full, t & 1, bars, a.status))) break;
+        kf::umma_commit(&bars->s_full[t & 1]);
+      };
+      bool ok = tc_wait(&bars->q_ready, 0, bars, a.status) &&
+                tc_wait(&bars->full[0], 0, bars, a.status);
+      if (ok) {
+        kf::tc_fence_after();
+        issue_qk(0);
+      }
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int s = t % kTcStages;
+        if (t + 1 < n_tiles) {
+          if (!(ok = tc_wait(&bars->full[(t + 1) % kTcStages], ((t + 1) / kTcStages) & 1, bars, a.status))) break;
+          kf::tc_fence_after();
+          issue_qk(t + 1);
+        }
+        if (!(ok = tc_wait(&bars->p_full[t & 1], (t >> 1) & 1, bars, a.status))) break;
         kf::tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTcKeys / 16; ++kk)
-          kf::umma_ts(tmem + 128, tmem + kk * 8, kf::sdesc_at(dv, koff + kk * 2048), idesc_pv,
-                      (t > 0 || kk > 0));
+          kf::umma_ts(tmem + 128, tmem + (t & 1) * kTcKeys + kk * 8, kf::sdesc_at(dv, s * TILE + kk * 2048),
+                      idesc_pv, (t > 0 || kk > 0));
         kf::umma_commit(&bars->empty[s]);
+        kf::umma_commit(&bars->pv_done);
       }
       kf::umma_commit(&bars->o_done);
     }
@@ -669,7 +693,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
         const bool ok = in && c * 8 < a.D;
-        kf::cp_async16(sQ + (c >> 3) * PANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4), src + (ok ? c * 8 : 0), ok);
+        kf::cp_async16(sQ + (c >> 3) * QPANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4), src + (ok ? c * 8 : 0), ok);
       }
       kf::cp_async_commit();
       kf::cp_async_wait<0>();
@@ -682,24 +706,23 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
     bool ok = true;
     if (warp < active_warps) {
       for (int t = 0; ok && t < n_tiles; ++t) {
-        if (!(ok = tc_wait(&bars->s_full, t & 1, bars, a.status))) break;
+        if (!(ok = tc_wait(&bars->s_full[t & 1], (t >> 1) & 1, bars, a.status))) break;
         kf::tc_fence_after();
-        uint32_t sr[128];
-        kf::tmem_ld32(lane_base + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        kf::tmem_ld32(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-        kf::tmem_ld32(lane_base + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-        kf::tmem_ld32(lane_base + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        const uint32_t s_col = (t & 1) * kTcKeys;
+        uint32_t sr[kTcKeys];
+        kf::tmem_ld32(lane_base + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        kf::tmem_ld32(lane_base + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         kf::tmem_wait_ld();
         const int key0 = key_begin + t * kTcKeys;
         const int lim = key_end - key0;  // keys past the split's end are masked
         if (lim < kTcKeys) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < kTcKeys; ++c)
             if (c >= lim) sr[c] = 0xFF800000u;
         }
         float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 128; c += 8) {
+        for (int c = 0; c < kTcKeys; c += 8) {
           a0 = kf::fmax3(a0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
           a1 = kf::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
           a2 = kf::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
@@ -717,20 +740,27 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
         }
         const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
         l_sum *= alpha;
-        uint32_t pk[64];
-        float sum = 0.f;
+        const uint64_t scl = kf::f2(a.scale_log2, a.scale_log2), negm = kf::f2(-m_use, -m_use);
+        uint32_t pk[kTcKeys / 2];
+        uint64_t acc[2] = {0ull, 0ull};
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p0 = kf::ex2(__uint_as_float(sr[2 * c]) * a.scale_log2 - m_use);
-          const float p1 = kf::ex2(__uint_as_float(sr[2 * c + 1]) * a.scale_log2 - m_use);
-          sum += p0 + p1;
+        for (int c = 0; c < kTcKeys / 2; ++c) {
+          float x0, x1;
+          kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+          const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
+          acc[c & 1] = kf::add2(acc[c & 1], kf::f2(p0, p1));
           pk[c] = kf::pack2<BF16>(p0, p1);
         }
-        l_sum += sum;
-        kf::tmem_st32(lane_base + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-        kf::tmem_st32(lane_base + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        {
+          float s0, s1;
+          kf::f2_split(kf::add2(acc[0], acc[1]), s0, s1);
+          l_sum += s0 + s1;
+        }
+        kf::tmem_st32(lane_base + s_col, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
         if (__any_sync(0xffffffffu, rescale_o)) {
-          // O row *= alpha; the S commit of this tile covers the previous PV
+          // O row *= alpha once PV_{t-1} has landed (S_t was issued before it)
+          if (!(ok = tc_wait(&bars->pv_done, (t - 1) & 1, bars, a.status))) break;
+          kf::tc_fence_after();
           for (int c0 = 0; c0 < d_pad16; c0 += 16) {
             uint32_t orow[16];
             kf::tmem_ld16(lane_base + 128 + c0, orow);
@@ -742,7 +772,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
         }
         kf::tmem_wait_st();
         kf::tc_fence_before();
-        kf::mbar_arrive(&bars->p_full);
+        kf::mbar_arrive(&bars->p_full[t & 1]);
       }
       // ---------------------------------------------------------- epilogue
       if (ok && tc_wait(&bars->o_done, 0, bars, a.status)) {
@@ -1008,7 +1038,7 @@ template <bool BF16, int KS>
 int launch_tc(const DecodeArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
   constexpr int NP = KS > 4 ? 2 : 1;
   constexpr size_t TILE = (size_t)NP * kTcKeys * 128;
-  const size_t smem = 1024 + (2 * kTcStages + 1) * TILE + sizeof(TcBarriers);
+  const size_t smem = 1024 + 2 * kTcStages * TILE + (size_t)NP * 128 * 128 + sizeof(TcBarriers);
   auto kern = decode_tc_kernel<BF16, NP, KS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_decode: cannot reserve %zu bytes of shared memory", smem);
