@@ -298,7 +298,10 @@ def bench_prefill_e2e(args, world, rank, dtype):
 
     run(max(2, args.warmup))
     torch.cuda.synchronize()
-    steps = max(4, args.steps // 2)
+    # the same K steps as the device-resident leg: the pipeline fill (first
+    # copy in) and drain (last copy out) lie in the timed region and amortise
+    # over K, as they would over a training run
+    steps = max(4, args.steps)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
