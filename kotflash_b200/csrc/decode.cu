@@ -1545,6 +1545,9 @@ template <bool BF16>
 __global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(MergeArgs m, uint8_t* mailbox,
                                                                     int world, int32_t* status) {
   __shared__ int s_ok;
+  // the next kernel (a following decode call's split kernel) may set up while
+  // this merge waits for the peers; it waits for this grid before any access
+  kf::griddep_launch_dependents();
   const PeerLayout L = peer_layout(world, m.rows, m.D);
   uint32_t* ctrl = reinterpret_cast<uint32_t*>(mailbox);
   const uint32_t e = current_epoch(mailbox);
