@@ -1390,9 +1390,11 @@ extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const
 // launch, each rank owns a mailbox in its own memory that every peer can
 // write (CUDA IPC mapping, peer access over NVLink/NVSwitch; no multicast):
 //   put:   this rank's partial rows are stored (fp32) into slot [rank] of
-//          every rank's mailbox with plain peer stores; after each piece the
-//          sender adds the piece's row count to the receiver's arrival
-//          counter with a system-scope release reduction;
+//          every rank's mailbox with plain peer stores; then the sender adds
+//          the row count to the receiver's arrival counter with release
+//          semantics at system scope (a release reduction per piece in
+//          kf_decode_peer_put; a system fence plus a relaxed reduction per
+//          receiver, from parallel lanes, in the fused kv-split entry);
 //   merge: every CTA waits (bounded) until its mailbox's counter shows all
 //          W x rows rows of this call, then merges the W partials (the
 //          split-merge math).
@@ -1405,13 +1407,15 @@ extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const
 // halves alternate by epoch parity; a rank cannot write epoch e + 2 into a
 // half before every peer has finished merging epoch e from it (its merge of
 // e + 1 needs their rows of e + 1, sent after their merge of e in stream
-// order).  Counters only grow: after epoch e the counter of half (e & 1)
-// holds W * rows * ((e + 1) / 2) modulo 2^32, and no intermediate value of
-// an epoch equals it.
+// order; with programmatic dependent launch every kernel of the next call
+// still waits for the previous grid to complete before its first access).
+// Counters only grow: after epoch e the counter of half (e & 1) holds
+// W * rows * ((e + 1) / 2) modulo 2^32, and no intermediate value of an
+// epoch equals it.
 //
 // Mailbox layout: [0, 256) control words {completed epochs, merge ticket,
-// send ticket},
-// then two halves of {O [W][rows][D] fp32, LSE [W][rows] fp32, counter}.
+// send ticket}, then two halves of {O [W][rows][D] fp32, LSE [W][rows] fp32,
+// counter}.
 namespace {
 
 constexpr int kMaxPeers = 8;
