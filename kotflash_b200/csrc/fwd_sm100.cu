@@ -14,6 +14,9 @@
 //   warp  8    TMA producer (Q once, then K/V blocks of 128 keys)
 //   warp  9    TMEM allocator + tcgen05.mma issuer for tile 0
 //   warp 10    tcgen05.mma issuer for tile 1
+//   warp 11    spare (completes the third warpgroup)
+// The softmax warpgroups raise their register limit to 224 (setmaxnreg) and
+// warps 8-11 lower theirs to 56, which removes most softmax spills (+2%).
 // Tensor memory (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P (16-bit) overwrites the first 64 columns of its S tile and feeds the
 // PV product directly from TMEM (A operand in tensor memory).
@@ -42,7 +45,11 @@ namespace {
 
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;  // 3 warpgroups: two softmax, one producer + MMA issuers + spare
+// Register split between the warpgroups (setmaxnreg): a softmax thread holds a
+// 128-column score row and its packed probabilities, the other roles little.
+// 256 * 224 + 128 * 56 = 384 * 168, the allocation the block launches with.
+constexpr int kRegSoftmax = 224, kRegOther = 56;
 constexpr int kStages = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -191,7 +198,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   // barrier phases run on across items (g counts K/V blocks of all items,
   // it counts items).
   const int rounds = (p.n_items + (int)gridDim.x - 1) / (int)gridDim.x;
-  if (warp == 8) {
+  if (warp >= 8) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegOther));
+   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int g = 0, it = 0;
@@ -310,7 +319,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         ++it;
       }
     }
+   }
+   // warp 11 is spare: it completes the third warpgroup for the register split
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegSoftmax));
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;        // tile handled by this warpgroup
     const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
@@ -485,6 +497,12 @@ int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: cannot reserve %zu bytes of shared memory", smem);
+  // setmaxnreg.inc waits until the block's launch allocation covers the
+  // split, so refuse to launch if the compiler allocated less than that.
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
+      fa.numRegs * kThreads < 256 * kRegSoftmax + 128 * kRegOther)
+    return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: register split does not fit (%d registers)", fa.numRegs);
   const int grid = std::min(p.n_items, kf::sm_count_current_device());
   kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, p);
   return kf::check_launch("kf_attn_fwd");
