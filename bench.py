@@ -12,19 +12,30 @@ Sq=Sk=4096, D=128, bf16, q scaled by 1/sqrt(D), through the public
 32 units of one full config (global batch 4*N), so the scaling is weak.
 FLOPs count only visible (q, k) pairs: fwd 4*B*Hq*D*P, bwd 2.5x fwd.
 
-Also reported, in the same JSON line:
-  * ``decode``: split-KV decode sweep (B2 Hq8 Hkv2 D64 fp16, Sq 1/4/16, Sk up
-    to 131072) in us/token and HBM GB/s, timed as CUDA-graph replays over
-    rotating K/V copies (working set > 3x L2); the KV-cache loop (capacity
-    32768, B8 Hq32 Hkv8 D128 bf16, 4096-token prefill append then 256 fused
-    append+decode steps in one CUDA graph);
-  * ``decode_multi_gpu`` (N > 1): Sk=131072 split across ranks, one NCCL
-    all-gather of packed (O, LSE) partials, merge; compute and exchange
-    timed separately, max over ranks.
+Output: detail lines first (``{"detail": ...}``: the decode sweep, the
+odd-head-dim runs, the GPU comparators, the decoder-block step), then the
+headline JSON line LAST, which also carries compact summaries:
+  * ``parity``: max |err| of O, LSE, dQ, dK, dV against a chunked fp32
+    reference computed on the GPU (cfg2 bf16 and fp16 batch 0, cfg5 one unit
+    at S=16384 for D72/96 causal and not, cfg3 Sq 1/16 at Sk=131072) and the
+    bit-exactness of the cache appends (cfg4), tolerance atol=rtol=2e-2;
+  * ``fp16``: the fp16 variant of the prefill config;
+  * ``cfg5``: the odd-head-dim training config (B2 Hq16 Hkv4 S16384 D72/96
+    fp16) sharded by (batch x KV head) units over the ranks (strong scaling);
+  * ``decode``: split-KV decode (B2 Hq8 Hkv2 D64 fp16) Sq=1 points, the
+    Sq=4/16 points at Sk=32768/131072, and the KV-cache loop (capacity
+    32768, B8 Hq32 Hkv8 D128 bf16, 256 fused append+decode steps in one CUDA
+    graph);
+  * ``decode_multi_gpu`` (N > 1): Sk=131072 split across ranks, NVLink
+    peer-memory exchange and NCCL all-gather, with max_err against an fp32
+    reference over the full sequence;
+  * ``e2e``: the step through the public API with host inputs and outputs,
+    and ``copy_bound``, the same copies alone with all ranks copying at once;
   * ``cpu_baseline``: the reference's CPU route (PyTorch SDPA + autograd,
     restated in oracle/) on one (batch, KV-head) unit on the host cores.
 
-``--impl reference`` runs only that CPU route (rank 0; other ranks exit).
+``--impl reference`` runs only that CPU route on the full config (rank 0;
+other ranks exit at once, no process group).
 """
 from __future__ import annotations
 
@@ -311,7 +322,158 @@ def bench_prefill_e2e(args, world, rank, dtype):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
-    return ms, h2d, d2h
+
+    # The bound on that number: the same copies with no compute, both
+    # directions at once, every rank copying at the same time (the host's
+    # memory and PCIe fabric are shared by the ranks).
+    outs_d = [tuple(torch.empty_like(h, device="cuda") for h in outs_h[j]) for j in range(2)]
+
+    def copies(n):
+        s_in.wait_stream(comp)
+        s_out.wait_stream(comp)
+        for i in range(n):
+            j = i % 2
+            with torch.cuda.stream(s_in):
+                for d, h in zip(dev[j], hosts[j]):
+                    d.copy_(h, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                for h, d in zip(outs_h[j], outs_d[j]):
+                    h.copy_(d, non_blocking=True)
+        comp.wait_stream(s_in)
+        comp.wait_stream(s_out)
+
+    copies(2)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(comp)
+    copies(steps)
+    end.record(comp)
+    torch.cuda.synchronize()
+    barrier(world)
+    copy_ms = max_over_ranks(start.elapsed_time(end), world) / steps
+    return ms, h2d, d2h, copy_ms
+
+
+# --------------------------------------------------------------------------- parity
+PARITY_TOL = 2e-2  # atol = rtol, BASELINE north star (fp16/bf16 vs an fp32 reference)
+
+
+def fp32_attention_reference(q, k, v, do=None, *, causal, scale, chunk=1024):
+    """Plain fp32 attention on the GPU, one query head and ``chunk`` query rows
+    at a time: (O, LSE) and, with ``do``, (dQ, dK, dV) by the standard
+    formulas (P = exp(S - LSE), dS = P (dO V^T - rowsum(O dO)), dQ = scale dS K,
+    dK = scale dS^T Q, dV = P^T dO, summed over each KV head's query heads).
+    The checker for the parity block; nothing here is timed."""
+    b, hq, sq, d = q.shape
+    hkv, sk = k.shape[1], k.shape[2]
+    group = hq // hkv
+    dev = q.device
+    o = torch.empty(b, hq, sq, d, device=dev)
+    lse = torch.empty(b, hq, sq, device=dev)
+    grads = do is not None
+    if grads:
+        dq = torch.empty(b, hq, sq, d, device=dev)
+        dk = torch.zeros(b, hkv, sk, d, device=dev)
+        dv = torch.zeros(b, hkv, sk, d, device=dev)
+    kpos = torch.arange(sk, device=dev)[None, :]
+    for bi in range(b):
+        for h in range(hq):
+            g = h // group
+            kh, vh = k[bi, g].float(), v[bi, g].float()
+            for r0 in range(0, sq, chunk):
+                r1 = min(sq, r0 + chunk)
+                qc = q[bi, h, r0:r1].float()
+                s = (qc @ kh.t()) * scale
+                if causal:
+                    s = s.masked_fill(kpos > torch.arange(r0, r1, device=dev)[:, None], float("-inf"))
+                l = torch.logsumexp(s, dim=-1)
+                p = torch.nan_to_num(torch.exp(s - l[:, None]), nan=0.0)
+                oc = p @ vh
+                o[bi, h, r0:r1] = oc
+                lse[bi, h, r0:r1] = l
+                if grads:
+                    dc = do[bi, h, r0:r1].float()
+                    ds = p * (dc @ vh.t() - (oc * dc).sum(-1, keepdim=True))
+                    dq[bi, h, r0:r1] = (ds @ kh) * scale
+                    dk[bi, g] += (ds.t() @ qc) * scale
+                    dv[bi, g] += p.t() @ dc
+    return (o, lse, dq, dk, dv) if grads else (o, lse)
+
+
+def max_err(got, want):
+    """(max |got - want|, max |got - want| / (atol + rtol |want|)) over finite entries."""
+    a, e = got.float(), want.float()
+    fin = torch.isfinite(e)
+    if not bool(torch.equal(torch.isfinite(a), fin)):
+        return float("inf"), float("inf")
+    diff = (a - e).abs()[fin]
+    if diff.numel() == 0:
+        return 0.0, 0.0
+    return diff.max().item(), (diff / (PARITY_TOL + PARITY_TOL * e.abs()[fin])).max().item()
+
+
+def _sig(x):
+    return float(f"{x:.3g}")
+
+
+def bench_parity():
+    """Max errors of the CUDA path against the fp32 reference at the BASELINE
+    configs, in the driver-kept record.  Returns {case: [errors]} plus the
+    worst error/tolerance ratio."""
+    from kotflash_b200.attention import _decode_forward, attention_backward, attention_forward
+
+    out = {"tol": PARITY_TOL, "fields": "O,LSE,dQ,dK,dV"}
+    worst = 0.0
+
+    def record(name, pairs):
+        nonlocal worst
+        errs = []
+        for got, want in pairs:
+            e, r = max_err(got, want)
+            errs.append(_sig(e))
+            worst = max(worst, r)
+        out[name] = errs
+
+    # cfg2 at full size, both dtypes; the reference on batch 0 (32 heads)
+    for dt, name in ((torch.bfloat16, "cfg2_bf16"), (torch.float16, "cfg2_fp16")):
+        q, k, v, do = make_prefill_inputs(dt, 555, "cuda")
+        d = CFG["D"]
+        o, lse = attention_forward(q, k, v, causal=True, scale=d ** -0.5)
+        dq, dk, dv = attention_backward(q, k, v, o, lse, do, causal=True, scale=d ** -0.5)
+        ref = fp32_attention_reference(q[:1], k[:1], v[:1], do[:1], causal=True, scale=d ** -0.5)
+        record(name, zip((o[:1], lse[:1], dq[:1], dk[:1], dv[:1]), ref))
+        del q, k, v, do, o, lse, dq, dk, dv, ref
+        torch.cuda.empty_cache()
+    # cfg5: one (batch, KV-head) unit at the full 16384 length
+    s = 16384
+    for d in (72, 96):
+        g = torch.Generator(device="cuda").manual_seed(700 + d)
+        q = torch.randn(1, 4, s, d, device="cuda", generator=g).half()
+        k = torch.randn(1, 1, s, d, device="cuda", generator=g).half()
+        v = torch.randn(1, 1, s, d, device="cuda", generator=g).half()
+        do = torch.randn(1, 4, s, d, device="cuda", generator=g).half()
+        for causal in (False, True):
+            o, lse = attention_forward(q, k, v, causal=causal, scale=d ** -0.5)
+            dq, dk, dv = attention_backward(q, k, v, o, lse, do, causal=causal, scale=d ** -0.5)
+            ref = fp32_attention_reference(q, k, v, do, causal=causal, scale=d ** -0.5)
+            record(f"cfg5_d{d}_{'causal' if causal else 'full'}", zip((o, lse, dq, dk, dv), ref))
+        del q, k, v, do
+        torch.cuda.empty_cache()
+    # cfg3 at the longest visible length
+    g = torch.Generator(device="cuda").manual_seed(808)
+    k = torch.randn(2, 2, 131072, 64, device="cuda", generator=g).half()
+    v = torch.randn(2, 2, 131072, 64, device="cuda", generator=g).half()
+    for sq in (1, 16):
+        q = torch.randn(2, 8, sq, 64, device="cuda", generator=g).half()
+        o, lse = _decode_forward(q, k, v, scale=0.125, want_lse=True)
+        ref = fp32_attention_reference(q, k, v, causal=False, scale=0.125)
+        record(f"cfg3_sq{sq}_sk131072", zip((o, lse), ref))
+    del k, v
+    torch.cuda.empty_cache()
+    out["worst_err_over_tol"] = _sig(worst)
+    out["pass"] = worst <= 1.0
+    return out
 
 
 # --------------------------------------------------------------------------- decode
@@ -378,7 +540,9 @@ def bench_cache_loop(peaks):
     # prefill append bandwidth (K4), timed as graph replays of the same append
     ms_app = _graph_time(lambda i: _append_at(cache, pk, pv, 0), 8)
     app_bytes = 2 * 2 * pk.numel() * 2  # read new K,V + write cache K,V
-    cache.append(pk, pv)
+    torch.cuda.synchronize()
+    prefill_exact = bool(torch.equal(cache.k[:, :, :pre], pk) and torch.equal(cache.v[:, :, :pre], pv))
+    cache.length = pre
     # prefill attention reading the cache's strided prefix view in place (K1), the
     # reference example's prefill -> decode handoff (examples/gqa_kv_cache_decode.py:58-65)
     from kotflash_b200 import attention
@@ -405,6 +569,10 @@ def bench_cache_loop(peaks):
 
     ms = _graph_time(one, steps, replays=3)
     cache.length = base + steps
+    torch.cuda.synchronize()
+    # every replay wrote step i's row at base + i with the fused append (K3)
+    loop_exact = bool(torch.equal(cache.k[:, :, base:base + steps], nk[:, :, :, 0].permute(1, 2, 0, 3))
+                      and torch.equal(cache.v[:, :, base:base + steps], nv[:, :, :, 0].permute(1, 2, 0, 3)))
     mean_len = base + (steps + 1) / 2
     step_bytes = 2 * b * hkv * mean_len * d * 2 + 2 * b * hq * d * 2 + 2 * b * hkv * d * 2
     gbs = step_bytes / (ms * 1e-3) / 1e9
@@ -420,6 +588,7 @@ def bench_cache_loop(peaks):
         "loop_ms": round(ms * steps, 3), "hbm_gbs": round(gbs, 1),
         "hbm_frac": round(gbs / peaks["hbm_gbs"], 3),
         "note": "fused append+decode, 256 steps in one CUDA graph; working set 134-143 MB (> L2)",
+        "append_bit_exact": {"prefill_append_kernel": prefill_exact, "fused_append_256_steps": loop_exact},
     }
 
 
@@ -429,36 +598,64 @@ def _append_at(cache, k, v, start):
     append_kv_cuda(cache.k, cache.v, k, v, start)
 
 
-def bench_odd_head_dim(peaks):
-    """B2 Hq16 Hkv4 S16384 fp16, D in {72, 96}, fwd+bwd, 1 GPU."""
+def bench_odd_head_dim(peaks, world, rank, iters=3):
+    """B2 Hq16 Hkv4 S16384 fp16, D in {72, 96}, causal
+    and not, fwd+bwd.  The job's 8 (batch, KV-head) units are sharded over the
+    ranks with no communication (1 unit per rank at N=8: strong scaling);
+    every rank builds the same seeded full inputs and takes its units.  Time
+    = max over ranks of the CUDA-event time of the rank's units, mean of
+    ``iters`` runs after one warm-up."""
+    from kotflash_b200 import distributed as kd
     from kotflash_b200.attention import attention_backward, attention_forward
 
-    res = []
     b, hq, hkv, s = 2, 16, 4, 16384
+    group = hq // hkv
+    units = kd.shard_units(b, hkv, world, rank)
+    runs = kd.shard_slices(units, group)
+    res = []
     for d in (72, 96):
         g = torch.Generator(device="cuda").manual_seed(d)
-        q = torch.randn(b, hq, s, d, device="cuda", generator=g).half()
-        k = torch.randn(b, hkv, s, d, device="cuda", generator=g).half()
-        v = torch.randn(b, hkv, s, d, device="cuda", generator=g).half()
-        do = torch.randn(b, hq, s, d, device="cuda", generator=g).half()
+        full = [torch.randn(b, h, s, d, device="cuda", generator=g).half() for h in (hq, hkv, hkv, hq)]
+        parts = [tuple(t[bi:bi + 1, sl].contiguous() for t, sl in zip(full, (qs, kvs, kvs, qs)))
+                 for bi, kvs, qs in runs]
+        del full
+        torch.cuda.empty_cache()
         for causal in (False, True):
             scale = d ** -0.5
-            out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
-            attention_backward(q, k, v, out, lse, do, causal=causal, scale=scale)
+
+            def once(ev=None):
+                for q, k, v, do in parts:
+                    if ev is not None:
+                        ev[0].record()
+                    out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
+                    if ev is not None:
+                        ev[1].record()
+                    attention_backward(q, k, v, out, lse, do, causal=causal, scale=scale)
+                    if ev is not None:
+                        ev[2].record()
+
+            once()
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(iters)]
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world)
             torch.cuda.synchronize()
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-            ev[0].record()
-            out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
-            ev[1].record()
-            attention_backward(q, k, v, out, lse, do, causal=causal, scale=scale)
-            ev[2].record()
+            start.record()
+            for i in range(iters):
+                once(evs[i])
+            end.record()
             torch.cuda.synchronize()
+            barrier(world)
+            ms = max_over_ranks(start.elapsed_time(end) / iters, world)
             f = fwd_flops(b, hq, s, s, d, causal)
-            fm, bm = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
-            tf = 3.5 * f / ((fm + bm) * 1e-3) / 1e12
-            res.append({"d": d, "causal": causal, "fwd_ms": round(fm, 3), "bwd_ms": round(bm, 3),
-                        "fwd_bwd_tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 3)})
-        del q, k, v, do
+            tf = 3.5 * f / (ms * 1e-3) / 1e12
+            line = {"d": d, "causal": causal, "ms": round(ms, 3), "fwd_bwd_tflops": round(tf, 1),
+                    "per_rank_frac": round(tf / world / peaks["bf16_tflops"], 3),
+                    "units_per_rank": len(units)}
+            if len(parts) == 1:  # forward/backward split of this rank's one run
+                line["fwd_ms"] = round(statistics.mean(e[0].elapsed_time(e[1]) for e in evs), 3)
+                line["bwd_ms"] = round(statistics.mean(e[1].elapsed_time(e[2]) for e in evs), 3)
+            res.append(line)
+        del parts
         torch.cuda.empty_cache()
     return res
 
@@ -471,7 +668,9 @@ def bench_decode_multi_gpu(world, rank):
     compute-only part is captured separately so compute and exchange are
     reported apart.  Two exchanges: NVLink peer memory (``PeerExchange``, two
     kernels) and the NCCL route (pack, all-gather, merge).  Max over ranks of
-    device time per call."""
+    device time per call.  Correctness: every rank also holds the full K/V
+    and compares both routes' (O, LSE) with an fp32 reference over the whole
+    sequence; ``max_err`` is the max over ranks."""
     from kotflash_b200 import distributed as kd
     from kotflash_b200.attention import _decode_forward
 
@@ -484,6 +683,7 @@ def bench_decode_multi_gpu(world, rank):
         v_full = torch.randn(2, 2, sk, 64, device="cuda", generator=g).half()
         q = torch.randn(2, 8, sq, 64, device="cuda", generator=g).half()
         kl, vl = k_full[:, :, lo:hi].contiguous(), v_full[:, :, lo:hi].contiguous()
+        ref_o, ref_lse = fp32_attention_reference(q, k_full, v_full, causal=False, scale=0.125)
         del k_full, v_full
         try:
             ex = kd.PeerExchange(rows=q[..., 0].numel(), d=64, dtype=q.dtype)
@@ -500,6 +700,12 @@ def bench_decode_multi_gpu(world, rank):
             _decode_forward(q, kl, vl, scale=0.125, want_lse=True)
 
         barrier(world)
+        o_n, l_n = kd.decode_kv_split(q, kl, vl, scale=0.125)
+        err_n = max(max_err(o_n, ref_o)[0], max_err(l_n, ref_lse)[0])
+        if ex is not None:
+            o_p, l_p = kd.decode_kv_split(q, kl, vl, scale=0.125, exchange=ex)
+            err_p = max(max_err(o_p, ref_o)[0], max_err(l_p, ref_lse)[0])
+        barrier(world)
         t_n = _graph_time(nccl, 8, replays=5)
         if ex is not None:
             barrier(world)
@@ -508,20 +714,24 @@ def bench_decode_multi_gpu(world, rank):
         t_c = _graph_time(local, 8, replays=5)
         n = max_over_ranks(t_n, world)
         c = max_over_ranks(t_c, world)
+        err_n = max_over_ranks(err_n, world)
         if ex is not None:
             pp = max_over_ranks(t_p, world)
+            err_p = max_over_ranks(err_p, world)
             timeouts = max_over_ranks(float(ex.status()), world)
             barrier(world)
             ex.close()
             peer_line = {"exchange_merge_us": round((pp - c) * 1e3, 2), "total_us": round(pp * 1e3, 2),
-                         "us_per_token": round(pp * 1e3 / sq, 3), "timeouts": int(timeouts)}
+                         "us_per_token": round(pp * 1e3 / sq, 3), "timeouts": int(timeouts),
+                         "max_err": _sig(err_p)}
         else:
             peer_line = {"unavailable": peer_error}
         out.append({"sq": sq, "sk": sk, "ranks": world, "keys_per_rank": hi - lo,
                     "compute_us": round(c * 1e3, 2),
                     "peer": peer_line,
                     "nccl": {"exchange_merge_us": round((n - c) * 1e3, 2), "total_us": round(n * 1e3, 2),
-                             "us_per_token": round(n * 1e3 / sq, 3)},
+                             "us_per_token": round(n * 1e3 / sq, 3), "max_err": _sig(err_n)},
+                    "max_err_tol": PARITY_TOL,
                     "timing": "CUDA-graph replay, max over ranks"})
         torch.cuda.synchronize()
     return out
@@ -746,22 +956,33 @@ def cpu_unit_sample(dtype_name: str, budget_s: float = 12.0, min_runs: int = 1):
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's CPU route on the host cores (rank 0 only)."""
+    """--impl reference: the reference's CPU route on the host cores, rank 0 only.
+
+    At N=1 every step is the full prefill config (B4 Hq32 Hkv8 S4096 D128
+    bf16, causal, forward + autograd backward through PyTorch SDPA with native
+    GQA, as ``backend="sdpa"`` runs it).  At N>1 the job (global batch 4N) is
+    far beyond a bounded CPU run, so each step is one (batch, KV-head) unit of
+    it and ``ms_per_step`` is that unit's measured time.  Throughput in
+    TFLOP/s counts the same visible-pair FLOPs as the GPU arm."""
     if rank != 0:
         return 0
     use_all_host_cores()
-    g = torch.Generator().manual_seed(0)
     from oracle import attention_oracle as oracle
 
-    group = CFG["Hq"] // CFG["Hkv"]
-    s, d = CFG["S"], CFG["D"]
-    q = (torch.randn(1, group, s, d, generator=g) * d ** -0.5).bfloat16()
-    k = torch.randn(1, 1, s, d, generator=g).bfloat16()
-    v = torch.randn(1, 1, s, d, generator=g).bfloat16()
-    do = torch.randn(1, group, s, d, generator=g).bfloat16()
+    g = torch.Generator().manual_seed(0)
+    b, hq, hkv, s, d = CFG["B"], CFG["Hq"], CFG["Hkv"], CFG["S"], CFG["D"]
+    group = hq // hkv
+    full = world == 1
+    shape_q = (b, hq, s, d) if full else (1, group, s, d)
+    shape_k = (b, hkv, s, d) if full else (1, 1, s, d)
+    q = (torch.randn(*shape_q, generator=g) * d ** -0.5).bfloat16()
+    k = torch.randn(*shape_k, generator=g).bfloat16()
+    v = torch.randn(*shape_k, generator=g).bfloat16()
+    do = torch.randn(*shape_q, generator=g).bfloat16()
     dtn = "bf16"
     try:
-        oracle.sdpa_reference_route(q[:, :, :256], k[:, :, :256], v[:, :, :256], do[:, :, :256], causal=True)
+        oracle.sdpa_reference_route(q[:1, :group, :256], k[:1, :1, :256], v[:1, :1, :256], do[:1, :group, :256],
+                                    causal=True)
     except RuntimeError:
         q, k, v, do = (t.float() for t in (q, k, v, do))
         dtn = "fp32"
@@ -772,21 +993,23 @@ def run_reference(args, world, rank):
         t0 = time.perf_counter()
         oracle.sdpa_reference_route(q, k, v, do, causal=True)
         times.append(time.perf_counter() - t0)
-    per_unit = statistics.median(times)
-    unit_flops = 3.5 * fwd_flops(1, group, s, s, d, True)
-    tflops = unit_flops / per_unit / 1e12
-    units = CFG["B"] * CFG["Hkv"] * world
+    per_step = statistics.median(times)
+    step_flops = 3.5 * fwd_flops(shape_q[0], shape_q[1], s, s, d, True)
+    tflops = step_flops / per_step / 1e12
+    sample = ("the full config per step" if full else
+              f"1 (batch, kv-head) unit of the job's {b * hkv * world} per step")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(per_unit * units * 1e3, 3), "higher_is_better": True,
+        "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dtn, "data": "synthetic",
-        "config": {"workload": "GQA causal prefill fwd+bwd B4 Hq32 Hkv8 S4096 D128 per rank",
-                   "global_batch": 4 * world, "seq_len": s, "parallelism": f"units{world}",
-                   "sample": "one (batch, kv-head) unit per step, extrapolated to the job"},
+        "config": {"workload": "GQA causal prefill fwd+bwd B4 Hq32 Hkv8 S4096 D128 per rank "
+                               "(BASELINE configs[1])",
+                   "global_batch": 4 * world, "seq_len": s, "head_dim": d,
+                   "parallelism": "host CPU cores (rank 0 only)", "sample": sample},
         "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": f"1 of {units} units per step ({dtn}), "
-                         "reference backend='sdpa' route + autograd"},
+                         "kind": "port", "sample": f"{sample} ({dtn}): reference backend='sdpa' route "
+                                                   "(PyTorch SDPA, native GQA) + autograd"},
         "e2e": {"value": round(tflops, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -822,6 +1045,24 @@ def run_decode_case(args, world, rank):
 
 
 # --------------------------------------------------------------------------- main
+def detail(name, payload):
+    """A detail line (no "metric" key): printed before the headline line."""
+    print(json.dumps({"detail": name, "data": payload}), flush=True)
+
+
+def bench_fp16_prefill(args, world, peaks):
+    """The fp16 variant of the prefill config (same step, same timing rules)."""
+    ns = argparse.Namespace(steps=args.steps, warmup=args.warmup, no_clocks=True)
+    ms, fwd_ms, bwd_ms, _ = bench_prefill(ns, world, 0, 0, torch.float16)
+    b, hq, s, d = CFG["B"], CFG["Hq"], CFG["S"], CFG["D"]
+    f = fwd_flops(b, hq, s, s, d, True)
+    tf = world * 3.5 * f / (ms * 1e-3) / 1e12
+    return {"value": round(tf, 1), "ms_per_step": round(ms, 4),
+            "frac": round(tf / world / peaks["bf16_tflops"], 4),
+            "fwd_tflops": round(f / (fwd_ms * 1e-3) / 1e12, 1),
+            "bwd_tflops": round(2.5 * f / (bwd_ms * 1e-3) / 1e12, 1)}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -833,23 +1074,22 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity block")
     ap.add_argument("--no-comparators", action="store_true",
-                    help="skip timing PyTorch SDPA's own GPU backends")
+                    help="skip timing PyTorch SDPA's own GPU backends and the decoder block")
     ap.add_argument("--decode-case", default=None, metavar="SQ,SK",
                     help="time only the split-KV decode config (B2 Hq8 Hkv2 D64 fp16) at one "
                          "(Sq, Sk) with --warmup/--steps plain launches; prints one JSON line")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
 
-    world, rank, local = init_dist(args)
     if args.impl == "reference":
-        rc = run_reference(args, world, rank)
-        if world > 1:
-            import torch.distributed as dist
+        # CPU only: no process group, no GPU; ranks other than 0 exit at once
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, world, rank)
 
-            dist.destroy_process_group()
-        return rc
-
+    world, rank, local = init_dist(args)
     from kotflash_b200 import _ext
 
     _ext.load()  # fail loudly when the kernel library is missing
@@ -866,26 +1106,36 @@ def main(argv=None) -> int:
 
     e2e = None
     if not args.no_e2e:
-        e2e_ms, h2d, d2h = bench_prefill_e2e(args, world, rank, dtype)
+        e2e_ms, h2d, d2h, copy_ms = bench_prefill_e2e(args, world, rank, dtype)
         e2e = {"value": round(world * per_rank / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "ms_per_step": round(e2e_ms, 3)}
+               "ms_per_step": round(e2e_ms, 3),
+               "copy_bound": {"ms_per_step": round(copy_ms, 3),
+                              "tflops": round(world * per_rank / (copy_ms * 1e-3) / 1e12, 2),
+                              "agg_gbs": round(world * (h2d + d2h) / (copy_ms * 1e-3) / 1e9, 1),
+                              "frac": round(copy_ms / e2e_ms, 3),
+                              "note": "same H2D+D2H copies, no compute, all ranks at once"}}
 
     peak = peaks["bf16_tflops"]
     bwd_achieved = f_bwd / (bwd_ms * 1e-3) / 1e12
     fwd_achieved = f_fwd / (fwd_ms * 1e-3) / 1e12
-    traffic = load_traffic()
+    traffic = load_traffic() or {}
     roofline = {
         "bound": "tensor", "kernel": "kf_attn_bwd (prep + main + finish launches)",
         "achieved": round(bwd_achieved, 1), "peak": peak, "unit": "TFLOP/s",
         "frac": round(bwd_achieved / peak, 4),
-        "traffic": (traffic or {}).get("bwd_main_bytes_per_launch"),
+        "traffic": traffic.get("bwd_main_bytes_per_launch"),
+        "traffic_source": traffic.get("source"),
         "peak_source": f"{peaks['source']} (burst bf16 cuBLAS)",
         "forward": {"kernel": "kf_attn_fwd", "achieved": round(fwd_achieved, 1),
                     "frac": round(fwd_achieved / peak, 4),
-                    "traffic": (traffic or {}).get("fwd_bytes_per_launch")},
+                    "traffic": traffic.get("fwd_bytes_per_launch")},
         "step_frac": round(value / world / peak, 4),
     }
+
+    fp16 = bench_fp16_prefill(args, world, peaks)
+    odd = bench_odd_head_dim(peaks, world, rank)
+    parity = bench_parity() if (rank == 0 and not args.no_parity) else None
 
     decode = None
     multi = None
@@ -894,7 +1144,6 @@ def main(argv=None) -> int:
             multi = bench_decode_multi_gpu(world, rank)
         elif rank == 0:
             decode = {"sweep": bench_decode_sweep(peaks), "kv_cache_loop": bench_cache_loop(peaks)}
-    odd = bench_odd_head_dim(peaks) if (rank == 0 and world == 1 and not args.no_decode) else None
     comparators = (bench_sdpa_comparators(dtype)
                    if (rank == 0 and world == 1 and not args.no_comparators) else None)
     block = bench_decoder_block() if (rank == 0 and world == 1 and not args.no_comparators) else None
@@ -908,6 +1157,28 @@ def main(argv=None) -> int:
                          f"backend='sdpa' route + autograd, {per_unit:.2f} s/unit"}
 
     if rank == 0:
+        if decode is not None:
+            detail("decode_sweep", decode["sweep"])
+        detail("odd_head_dim_training", odd)
+        if comparators is not None:
+            detail("gpu_comparators", comparators)
+        if block is not None:
+            detail("decoder_block_training_step", block)
+        if parity is not None and not parity["pass"]:
+            print("parity check FAILED: " + json.dumps(parity), file=sys.stderr, flush=True)
+        dec = None
+        if decode is not None:
+            keep = [r for r in decode["sweep"] if r["sq"] == 1 or r["sk"] >= 32768]
+            loop = decode["kv_cache_loop"]
+            dec = {"cols": "sq,sk,us_per_call,us_per_token,hbm_frac",
+                   "rows": [[r["sq"], r["sk"], r["us_per_call"], r["us_per_token"], r["hbm_frac"]] for r in keep],
+                   "kv_cache_loop": {"us_per_token": loop["us_per_token"], "hbm_frac": loop["hbm_frac"],
+                                     "prefill_append_hbm_frac": loop["prefill_append"]["hbm_frac"],
+                                     "append_bit_exact": loop["append_bit_exact"]}}
+        cfg5 = {"cols": "d,causal,ms,fwd_bwd_tflops,per_rank_frac",
+                "rows": [[r["d"], int(r["causal"]), r["ms"], r["fwd_bwd_tflops"], r["per_rank_frac"]]
+                         for r in odd],
+                "units_per_rank": odd[0]["units_per_rank"], "scaling": "strong (8 units over the ranks)"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -919,13 +1190,10 @@ def main(argv=None) -> int:
                        "parallelism": f"(batch x kv-head) units, {world} rank(s), no collective",
                        "l2": "inputs larger than L2 (q/dO 134 MB each)"},
             "frac_of_peak": round(value / world / peak, 4),
-            "roofline": roofline, "e2e": e2e, "clocks": clocks,
+            "roofline": roofline, "clocks": clocks,
             "gpu_launches": 4 * args.steps,
-            "cpu_baseline": cpu,
-            "decode": decode, "decode_multi_gpu": multi,
-            "odd_head_dim_training": odd,
-            "gpu_comparators": comparators,
-            "decoder_block_training_step": block,
+            "parity": parity, "fp16": fp16, "cfg5": cfg5, "decode": dec,
+            "decode_multi_gpu": multi, "e2e": e2e, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

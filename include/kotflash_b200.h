@@ -15,6 +15,13 @@
  * Device-side waits are bounded.  Kernels that give up on a wait write a
  * non-zero code into the caller-supplied `status` word (int32 in device
  * memory) and return; the host reads that word outside the hot path.
+ *
+ * Device: every entry point that takes device memory makes the GPU owning
+ * its first tensor (q, the K cache, o or the partials) current for the call
+ * and restores the caller's device before returning, as the reference's
+ * extension does with c10::cuda::CUDAGuard (kotflash/csrc/kv_append_cuda.cu:77).
+ * The stream must belong to that GPU.  kf_ipc_open_handle maps into the
+ * caller's current device.
  */
 #ifndef KOTFLASH_B200_H
 #define KOTFLASH_B200_H
@@ -120,9 +127,10 @@ int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
  * FFI embedder with a fixed device-memory budget) and gives plugins no
  * allocator.  Same arguments and results as kf_decode minus the workspace:
  * the split partials go to one file-scope device array of 8 MiB that every
- * GPU loading the library holds until exit.  The first call on a device
- * (with that device current) looks up the array's device address; make that
- * first call before any stream capture.  num_splits == 0 plans the split
+ * GPU loading the library holds until exit.  Each call looks up the array's
+ * address on the tensors' device (a host-side query, no allocation); the
+ * first call on a device also loads the module there, so make that first
+ * call before any stream capture.  num_splits == 0 plans the split
  * count and lowers it until the partials fit in 8 MiB; an explicit
  * num_splits whose partials (num_splits * B*Hq*Sq * (D+1) * 4 bytes) exceed
  * 8 MiB is rejected with KF_ERR_WORKSPACE.  All calls share the array: calls
@@ -177,8 +185,10 @@ int kf_merge_partials(const float* part_o, const float* part_lse, int num_splits
  * first, then the merges) without kernels that wait on one another.
  *
  * Every wait is bounded (about one second): on expiry *status (device
- * memory, may be null) = KF_DEV_TIMEOUT and the output is NaN; the mailboxes
- * must then be zeroed on every rank before the next call.  Every rank must
+ * memory, may be null) = KF_DEV_TIMEOUT and the output is NaN.  The exchange
+ * is then unusable: the timed-out half's arrival counter is short and a late
+ * sender's rows may still land in it, so every rank must stop calling, zero
+ * its mailbox (all ranks), and start again from a new set of mailboxes.  Every rank must
  * make the same sequence of calls with the same rows and D; the call count
  * is kept in the mailbox, so the launches may be captured in a CUDA graph
  * and replayed. */
@@ -209,6 +219,14 @@ int kf_decode_peer_merge(void* mailbox, int64_t rows, int64_t D, int dtype, int 
  * every attention kernel takes when a wait expires.  Used by the tests to
  * show that an expired wait is reported and leaves the context usable. */
 int kf_selftest_bounded_wait(int32_t* status, int64_t budget_us, void* stream);
+
+/* ---- self-test of the forward kernel's polynomial exponential -------------
+ * No counterpart in the reference (its Triton kernels call exp2 only).  The
+ * forward kernel computes part of its softmax exponentials on the fp32 pipe
+ * as a degree-3 polynomial after a Cody-Waite range split; this evaluates
+ * that same device function on n (even) fp32 arguments x (device memory) into
+ * y, so tests can bound its error against exp2 over the argument range. */
+int kf_selftest_exp2_poly(const float* x, float* y, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -68,6 +68,7 @@ SIGNATURES = {
     "kf_merge_partials": (_I, [_VP, _VP, _I, _I64, _I64, _VP, _VP, _I, _VP]),
     "kf_decode_noalloc": (_I, [_T4, _T4, _T4, _T4, _T4, _I64, _T4, _VP, _I, _F, _I, _VP]),
     "kf_selftest_bounded_wait": (_I, [_VP, _I64, _VP]),
+    "kf_selftest_exp2_poly": (_I, [_VP, _VP, _I64, _VP]),
     "kf_peer_mailbox_bytes": (_SZ, [_I, _I64, _I64]),
     "kf_ipc_get_handle": (_I, [_VP, _VP, ctypes.POINTER(ctypes.c_uint64)]),
     "kf_ipc_open_handle": (_I, [_VP, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),

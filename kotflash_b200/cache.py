@@ -78,6 +78,31 @@ def _kernel_append_ok(t: torch.Tensor) -> bool:
     return _kernel_device_ok(t) and t.dtype in (torch.float16, torch.bfloat16)
 
 
+_APPEND_OPT_IN = "KOTFLASH_ENABLE_CUDA_APPEND"
+
+
+def cuda_append_opted_in(env=None) -> bool:
+    """Whether ``append(backend="auto")`` may use the append kernel.
+
+    Same opt-in as the reference (``kotflash/cache.py:163-168``): only the
+    exact value ``"1"`` of ``KOTFLASH_ENABLE_CUDA_APPEND`` selects the kernel;
+    unset or any other value keeps the torch copies.  ``env`` overrides the
+    process environment (used by tests).
+    """
+    value = os.environ.get(_APPEND_OPT_IN) if env is None else env
+    return value == "1"
+
+
+def fused_append_auto_allowed(env=None) -> bool:
+    """Whether ``append_and_attend(append_backend="auto")`` may fuse the append.
+
+    The reference turns its fused route off when the append-kernel opt-in is
+    set (``kotflash/cache.py:248``): the caller then gets the separate append
+    kernel followed by attention.
+    """
+    return not cuda_append_opted_in(env)
+
+
 class PreallocatedKVCache:
     """Fixed-capacity K/V storage with append-only writes.
 
@@ -120,9 +145,8 @@ class PreallocatedKVCache:
 
         backend="torch" uses tensor ``copy_``; backend="cuda" forces the
         append kernel (fp16/bf16 on an sm_100 device); backend="auto" uses the
-        kernel for such tensors unless ``KOTFLASH_ENABLE_CUDA_APPEND=0``.  The
-        kernel library is prebuilt, so unlike the reference no opt-in is
-        needed to avoid a JIT compile.
+        kernel for such tensors only when ``KOTFLASH_ENABLE_CUDA_APPEND=1``,
+        the reference's opt-in, and the torch copies otherwise.
         """
         self._check_new(new_k, new_v)
         if backend not in {"auto", "torch", "cuda"}:
@@ -134,9 +158,7 @@ class PreallocatedKVCache:
                 f"exceeds max_len={self.max_len}"
             )
         use_cuda = backend == "cuda" or (
-            backend == "auto"
-            and os.environ.get("KOTFLASH_ENABLE_CUDA_APPEND", "1") != "0"
-            and _kernel_append_ok(self.k)
+            backend == "auto" and cuda_append_opted_in() and _kernel_append_ok(self.k)
         )
         if use_cuda:
             from ._cuda_append import append_kv_cuda
@@ -177,7 +199,9 @@ class PreallocatedKVCache:
         tensors) writes the new row inside the split-KV decode launch; every
         split substitutes the new row from new_k/new_v, so no CTA reads a row
         another CTA is writing (ref ``triton_decode.py:109-238``).
-        Grad-enabled calls use append + attention.
+        Grad-enabled calls use append + attention, and so does "auto" when
+        ``KOTFLASH_ENABLE_CUDA_APPEND=1`` asks for the append kernel (as the
+        reference routes it, ``kotflash/cache.py:248``).
         """
         if attention_backend not in {"auto", "triton", "sdpa"}:
             raise ValueError("attention backend must be one of: auto, triton or sdpa")
@@ -203,6 +227,7 @@ class PreallocatedKVCache:
         )
         use_fused = append_backend == "fused" or (
             append_backend == "auto" and fusable and not has_grad_inputs
+            and fused_append_auto_allowed()
         )
         if use_fused:
             if attention_backend == "sdpa":

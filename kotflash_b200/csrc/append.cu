@@ -78,6 +78,8 @@ extern "C" int kf_append(const kf_tensor4* k_cache, const kf_tensor4* v_cache,
     return set_error(KF_ERR_INVALID, "kf_append: append range exceeds cache capacity");
   if (!k_cache->ptr || !v_cache->ptr || !new_k->ptr || !new_v->ptr)
     return set_error(KF_ERR_INVALID, "kf_append: null data pointer");
+  kf::DeviceGuard guard(k_cache->ptr);
+  if (guard.status()) return guard.status();
 
   AppendArgs a;
   a.src_k = static_cast<const uint16_t*>(new_k->ptr);

@@ -727,6 +727,8 @@ extern "C" int kf_attn_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   const size_t need = kf_attn_bwd_workspace_bytes(B, Hq, Sq, D);
   if (!workspace || workspace_bytes < need)
     return set_error(KF_ERR_WORKSPACE, "kf_attn_bwd: workspace needs %zu bytes", need);
+  kf::DeviceGuard guard(q->ptr);
+  if (guard.status()) return guard.status();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == KF_BF16)
     return run_bwd<true>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, status, st);

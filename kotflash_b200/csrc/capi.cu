@@ -1,5 +1,6 @@
 // Library-wide C-ABI pieces: version, thread-local error text, TMA descriptor
 // encoding and the device-property cache.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -96,6 +97,34 @@ int encode_tmap_2d_f32(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, 
   return KF_OK;
 }
 
+DeviceGuard::DeviceGuard(const void* ptr) {
+  if (!ptr) return;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+    (void)cudaGetLastError();  // not a pointer the runtime knows: keep the current device
+    return;
+  }
+  if ((attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) || attr.device < 0) return;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) {
+    (void)cudaGetLastError();
+    rc_ = set_error(KF_ERR_CUDA, "cannot query the current CUDA device");
+    return;
+  }
+  if (cur == attr.device) return;
+  if (cudaSetDevice(attr.device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    rc_ = set_error(KF_ERR_CUDA, "cannot make device %d (the tensor's) current", attr.device);
+    return;
+  }
+  prev_ = cur;
+  switched_ = true;
+}
+
+DeviceGuard::~DeviceGuard() {
+  if (switched_) (void)cudaSetDevice(prev_);
+}
+
 int sm_count_current_device() {
   static int cache[64] = {0};
   int dev = 0;
@@ -130,6 +159,30 @@ static __global__ void selftest_wait_kernel(int32_t* status, uint64_t budget_ns)
 extern "C" int kf_selftest_bounded_wait(int32_t* status, int64_t budget_us, void* stream) {
   if (!status || budget_us <= 0 || budget_us > 10000000)
     return kf::set_error(KF_ERR_INVALID, "kf_selftest_bounded_wait: need a status word and 0 < budget_us <= 1e7");
+  kf::DeviceGuard guard(status);
+  if (guard.status()) return guard.status();
   selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, (uint64_t)budget_us * 1000u);
   return kf::check_launch("kf_selftest_bounded_wait");
+}
+
+// Evaluates the forward kernel's packed fp32-pipe exponential on pairs of
+// arguments: y[2i], y[2i+1] = exp2_poly2(x[2i], x[2i+1]).
+static __global__ void selftest_exp2_kernel(const float* x, float* y, int64_t pairs) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += (int64_t)gridDim.x * blockDim.x) {
+    float a, b;
+    kf::f2_split(kf::exp2_poly2(x[2 * i], x[2 * i + 1]), a, b);
+    y[2 * i] = a;
+    y[2 * i + 1] = b;
+  }
+}
+
+extern "C" int kf_selftest_exp2_poly(const float* x, float* y, int64_t n, void* stream) {
+  if (!x || !y || n <= 0 || n % 2)
+    return kf::set_error(KF_ERR_INVALID, "kf_selftest_exp2_poly: need x, y and an even n > 0");
+  kf::DeviceGuard guard(x);
+  if (guard.status()) return guard.status();
+  const int64_t pairs = n / 2;
+  const int64_t blocks = std::min<int64_t>((pairs + 255) / 256, 4096);
+  selftest_exp2_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, pairs);
+  return kf::check_launch("kf_selftest_exp2_poly");
 }

@@ -1255,6 +1255,9 @@ extern "C" int kf_decode(const kf_tensor4* q, const kf_tensor4* k, const kf_tens
                          const kf_tensor4* new_k, const kf_tensor4* new_v, int64_t past_len,
                          const kf_tensor4* o, float* lse, int dtype, float scale, int num_splits,
                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q) return kf::set_error(KF_ERR_INVALID, "kf_decode: null tensor descriptor");
+  kf::DeviceGuard guard(q->ptr);
+  if (guard.status()) return guard.status();
   DecodeArgs a;
   int rc = decode_setup(q, k, v, new_k, new_v, past_len, o, lse, dtype, scale, num_splits, workspace,
                         workspace_bytes, false, "kf_decode", a);
@@ -1279,6 +1282,8 @@ extern "C" int kf_merge_partials(const float* part_o, const float* part_lse, int
     return set_error(KF_ERR_INVALID, "kf_merge_partials: dtype must be fp16 or bf16");
   if ((reinterpret_cast<uintptr_t>(part_o) & 15) || (reinterpret_cast<uintptr_t>(o) & 7))
     return set_error(KF_ERR_INVALID, "kf_merge_partials: misaligned buffers");
+  kf::DeviceGuard guard(part_o);
+  if (guard.status()) return guard.status();
   MergeArgs m;
   m.part_o = part_o;
   m.part_lse = part_lse;
@@ -1306,10 +1311,13 @@ extern "C" int kf_merge_partials(const float* part_o, const float* part_lse, int
 // live in one file-scope device array of kNoAllocScratchBytes.  Every GPU that
 // loads this library holds that array until the process exits.
 //
-// Set-up: the first call on each device, with that device current, asks the
-// runtime for the array's device address (cudaGetSymbolAddress) and caches it
-// per device; make that first call before any stream capture.  Host code must
-// never pass the array's name to a kernel: on the host it is only a stand-in.
+// Set-up: every call, with the tensors' device current (the entry point makes
+// it so), asks the runtime for the array's device address on that device
+// (cudaGetSymbolAddress, a host-side lookup); nothing is cached, so the address
+// stays right if the device's primary context is torn down and recreated.  The
+// first call on a device also loads the module there, so make that first call
+// before any stream capture.  Host code must never pass the array's name to a
+// kernel: on the host it is only a stand-in.
 //
 // Sharing: all calls use the same array and it keeps the last call's
 // contents.  Nothing needs clearing (every split writes each of its partial
@@ -1322,21 +1330,14 @@ constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
 __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
 int noalloc_scratch(void** out) {
-  static std::mutex mu;
-  static void* ptrs[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
-    return kf::set_error(KF_ERR_CUDA, "kf_decode_noalloc: no current CUDA device");
-  std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || !p)
-      return kf::set_error(KF_ERR_CUDA, "kf_decode_noalloc: cudaGetSymbolAddress failed: %s",
-                           cudaGetErrorString(e));
-    ptrs[dev] = p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+  if (e != cudaSuccess || !p) {
+    (void)cudaGetLastError();
+    return kf::set_error(KF_ERR_CUDA, "kf_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                         cudaGetErrorString(e));
   }
-  *out = ptrs[dev];
+  *out = p;
   return KF_OK;
 }
 
@@ -1355,6 +1356,9 @@ extern "C" int kf_decode_noalloc(const kf_tensor4* q, const kf_tensor4* k, const
   const int64_t Hkv = k->size[1], Sk = k->size[2];
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0 || D <= 0)
     return kf::set_error(KF_ERR_INVALID, "kf_decode_noalloc: dimensions must be non-zero");
+  kf::DeviceGuard guard(q->ptr);
+  if (guard.status()) return guard.status();
+
   const size_t per_split = (size_t)(B * Hq * Sq) * (size_t)(D + 1) * sizeof(float);
   int64_t splits;
   if (num_splits > 0) {
@@ -1479,9 +1483,12 @@ __global__ void __launch_bounds__(kPeerThreads) peer_put_kernel(const uint16_t* 
                                                                 int D, int64_t rpp,
                                                                 const __grid_constant__ PeerSet peers, int world,
                                                                 int rank) {
-  kf::griddep_launch_dependents();  // the merge may launch now; it waits for the counter, not for this grid
   const PeerLayout L = peer_layout(world, rows, D);
+  // The epoch is read before this CTA lets the merge launch: the merge's last
+  // CTA advances it, and a dependent grid starts only once every CTA here has
+  // triggered, so no CTA of this grid can see the next call's epoch.
   const uint32_t e = current_epoch(peers.mailbox[rank]);
+  kf::griddep_launch_dependents();  // the merge waits for the counter, not for this grid
   const PeerHalf h = peer_half(peers.mailbox[blockIdx.y], L, e);
   const int64_t r0 = blockIdx.x * rpp, r1 = r0 + rpp < rows ? r0 + rpp : rows;
   if (r0 >= r1) return;
@@ -1661,6 +1668,9 @@ extern "C" size_t kf_peer_mailbox_bytes(int world, int64_t rows, int64_t D) {
 extern "C" int kf_ipc_get_handle(const void* ptr, void* handle, uint64_t* offset) {
   using kf::set_error;
   if (!ptr || !handle || !offset) return set_error(KF_ERR_INVALID, "kf_ipc_get_handle: null argument");
+  kf::DeviceGuard guard(ptr);
+  if (guard.status()) return guard.status();
+
   AddrRangeFn range = get_addr_range_fn();
   if (!range) return set_error(KF_ERR_CUDA, "kf_ipc_get_handle: cuMemGetAddressRange unavailable");
   CUdeviceptr base = 0;
@@ -1713,6 +1723,8 @@ extern "C" int kf_decode_peer_put(const void* o, const float* lse, int64_t rows,
   PeerSet peers;
   if ((rc = peer_set(what, mailboxes, world, rank, peers))) return rc;
   if (misaligned(o, 16) || misaligned(lse, 4)) return kf::set_error(KF_ERR_INVALID, "%s: misaligned buffers", what);
+  kf::DeviceGuard guard(o);
+  if (guard.status()) return guard.status();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t rpp = put_rows_per_piece(rows, (int)D);
   const dim3 grid((unsigned)((rows + rpp - 1) / rpp), world);
@@ -1733,6 +1745,8 @@ extern "C" int kf_decode_peer_merge(void* mailbox, int64_t rows, int64_t D, int 
   if (rc) return rc;
   if (misaligned(mailbox, 256) || misaligned(out, 8) || misaligned(out_lse, 4))
     return kf::set_error(KF_ERR_INVALID, "%s: misaligned buffers", what);
+  kf::DeviceGuard guard(out);
+  if (guard.status()) return guard.status();
   MergeArgs m = {};
   m.rows = rows;
   m.D = (int)D;
@@ -1792,6 +1806,9 @@ extern "C" int kf_decode_kv_split_peer_send(const kf_tensor4* q, const kf_tensor
                                             int dtype, float scale, int num_splits, void* workspace,
                                             size_t workspace_bytes, void* const* mailboxes, int world, int rank,
                                             void* stream) {
+  if (!q) return kf::set_error(KF_ERR_INVALID, "kf_decode_kv_split_peer_send: null tensor descriptor");
+  kf::DeviceGuard guard(q->ptr);
+  if (guard.status()) return guard.status();
   PeerSet peers;
   MergeArgs local;
   // no output here: q stands in for O's descriptor (shape checks only)
@@ -1804,6 +1821,9 @@ extern "C" int kf_decode_kv_split_peer(const kf_tensor4* q, const kf_tensor4* k,
                                        void* workspace, size_t workspace_bytes, void* const* mailboxes,
                                        int world, int rank, int32_t* status, void* stream) {
   const char* what = "kf_decode_kv_split_peer";
+  if (!q) return kf::set_error(KF_ERR_INVALID, "%s: null tensor descriptor", what);
+  kf::DeviceGuard guard(q->ptr);
+  if (guard.status()) return guard.status();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   PeerSet peers;
   MergeArgs m;

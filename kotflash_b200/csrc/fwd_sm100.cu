@@ -550,6 +550,8 @@ extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   if (!rows16(q) || !rows16(k) || !rows16(v) || !rows16(o))
     return set_error(KF_ERR_INVALID, "kf_attn_fwd: tensors need a contiguous last dim and 16-byte aligned rows");
 
+  kf::DeviceGuard guard(q->ptr);
+  if (guard.status()) return guard.status();
   const int box_inner = 64;
   CUtensorMap mq, mk, mv;
   int rc;

@@ -33,4 +33,26 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int sm_count_current_device();
 
+// Makes the GPU that owns `ptr` the current device for the guard's lifetime
+// and restores the caller's device afterwards, so an entry point launches,
+// encodes tensor maps and reads device properties on the tensor's own GPU
+// whatever device the calling thread has current (the C-ABI counterpart of
+// the reference extension's c10::cuda::CUDAGuard on its cache tensor,
+// kotflash/csrc/kv_append_cuda.cu:77).  A pointer the runtime does not know
+// (host memory, null) leaves the current device alone.  status() is KF_OK or
+// KF_ERR_CUDA with the message recorded.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(const void* ptr);
+  ~DeviceGuard();
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+  int status() const { return rc_; }
+
+ private:
+  int prev_ = -1;
+  bool switched_ = false;
+  int rc_ = 0;
+};
+
 }  // namespace kf

@@ -100,7 +100,11 @@ class PeerExchange:
     in the same order with the same shapes; the call count lives in device
     memory, so the call may be captured in a CUDA graph.  A bounded wait
     (about one second) guards every arrival: on expiry the output is NaN and
-    ``status()`` reports it, after which the exchange must be rebuilt.
+    ``status()`` reports it.  The exchange is then unusable (the timed-out
+    mailbox half is short of rows and a late sender may still write into it):
+    after ``status()`` has returned non-zero, ``decode`` and ``exchange``
+    raise, and every rank must ``close()`` it and build a new one, which
+    starts from zeroed mailboxes.
 
     Build it after ``init_process_group`` (it all-gathers the CUDA IPC
     handles); with no process group it is a one-rank exchange.  The mailbox
@@ -127,6 +131,7 @@ class PeerExchange:
         base = self.mailbox.data_ptr()
         self.local = (base + 255) // 256 * 256
         self.status_word = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._failed = False
         torch.cuda.synchronize(self.device)  # zeros land before any peer can write
         handle = (ctypes.c_uint8 * self.HANDLE_BYTES)()
         offset = ctypes.c_uint64(0)
@@ -169,6 +174,7 @@ class PeerExchange:
         (``kf_decode_kv_split_peer``): the split kernel, one kernel that
         merges this rank's splits and stores the fp32 result into every
         mailbox, and the final merge.  Returns the full (O, LSE)."""
+        self._check_usable()
         b, hq, sq, d = q.shape
         if q.dtype != self.dtype or d != self.d or b * hq * sq != self.rows:
             raise ValueError("PeerExchange.decode: q does not match the exchange's rows/d/dtype")
@@ -189,6 +195,7 @@ class PeerExchange:
 
     def exchange(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor = None,
                  out_lse: torch.Tensor = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        self._check_usable()
         if o.dtype != self.dtype or o.shape[-1] != self.d or o[..., 0].numel() != self.rows:
             raise ValueError("PeerExchange.exchange: o does not match the exchange's rows/d/dtype")
         if lse.numel() != self.rows or lse.dtype != torch.float32:
@@ -207,8 +214,19 @@ class PeerExchange:
         return out, out_lse
 
     def status(self) -> int:
-        """KF_DEV_TIMEOUT (1) once a wait expired, else 0 (synchronises)."""
-        return int(self.status_word.item())
+        """KF_DEV_TIMEOUT (1) once a wait expired, else 0 (synchronises).
+
+        A non-zero answer retires the exchange: later ``decode``/``exchange``
+        calls raise until a new ``PeerExchange`` replaces this one."""
+        s = int(self.status_word.item())
+        if s:
+            self._failed = True
+        return s
+
+    def _check_usable(self) -> None:
+        if self._failed:
+            raise RuntimeError("PeerExchange: a peer wait timed out; close() this exchange on every "
+                               "rank and build a new one (its mailboxes start zeroed)")
 
     def close(self) -> None:
         """Unmap the peers' mailboxes (every rank, after its last exchange)."""

@@ -101,6 +101,46 @@ def forward_backward(q, k, v, do, *, causal: bool, scale: Optional[float] = None
     return o, lse, dq, dk, dv
 
 
+def forward_backward_chunked(q, k, v, do, *, causal: bool, scale: Optional[float] = None,
+                             chunk: int = 1024):
+    """``forward_backward`` computed one query head and ``chunk`` query rows
+    at a time, so memory stays O(chunk x Sk) at long sequence lengths (the
+    16384-token training config).  Same formulas, fp32; returns
+    (O, LSE, dQ, dK, dV)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    b, hq, sq, d = q.shape
+    hkv, sk = k.shape[1], k.shape[2]
+    group = hq // hkv
+    dev = q.device
+    o = torch.empty(b, hq, sq, d, device=dev)
+    lse = torch.empty(b, hq, sq, device=dev)
+    dq = torch.empty(b, hq, sq, d, device=dev)
+    dk = torch.zeros(b, hkv, sk, d, device=dev)
+    dv = torch.zeros(b, hkv, sk, d, device=dev)
+    kpos = torch.arange(sk, device=dev)[None, :]
+    for bi in range(b):
+        for h in range(hq):
+            g = h // group
+            kh, vh = k[bi, g].float(), v[bi, g].float()
+            for r0 in range(0, sq, chunk):
+                r1 = min(sq, r0 + chunk)
+                qc, dc = q[bi, h, r0:r1].float(), do[bi, h, r0:r1].float()
+                s = torch.matmul(qc, kh.t()) * scale
+                if causal:
+                    s = s.masked_fill(kpos > torch.arange(r0, r1, device=dev)[:, None], float("-inf"))
+                l = torch.logsumexp(s, dim=-1)
+                p = torch.nan_to_num(torch.exp(s - l[:, None]), nan=0.0)
+                oc = torch.matmul(p, vh)
+                ds = p * (torch.matmul(dc, vh.t()) - (oc * dc).sum(-1, keepdim=True))
+                o[bi, h, r0:r1] = oc
+                lse[bi, h, r0:r1] = l
+                dq[bi, h, r0:r1] = torch.matmul(ds, kh) * scale
+                dk[bi, g] += torch.matmul(ds.t(), qc) * scale
+                dv[bi, g] += torch.matmul(p.t(), dc)
+    return o, lse, dq, dk, dv
+
+
 def split_partials(q, k, v, *, scale: float, bounds: Sequence[Tuple[int, int]]):
     """Per-split (O normalised, LSE) over key ranges ``bounds`` (non-causal)."""
     outs, lses = [], []

@@ -23,6 +23,21 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """One line with the largest measured error of the run's oracle checks."""
+    try:
+        from tests._util import RECORDS
+    except ImportError:
+        return
+    if not RECORDS:
+        return
+    name, err, _ = max(RECORDS, key=lambda r: r[1])
+    rname, rerr, ratio = max(RECORDS, key=lambda r: r[2])
+    terminalreporter.write_line(
+        f"[parity] {len(RECORDS)} checks vs the fp32 oracle (atol=rtol=2e-2): largest max_abs_err "
+        f"{err:.3e} ({name}); closest to tolerance {ratio:.2f} of it ({rname}, {rerr:.3e})")
+
+
 @pytest.fixture(autouse=True)
 def _device_wait_status(request):
     """GPU tests must finish with no expired device-side wait."""

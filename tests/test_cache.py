@@ -157,3 +157,29 @@ def test_cache_sequence_matches_reference_golden():
     assert torch.equal(uk, t["ds_uk"]) and torch.equal(uv, t["ds_uv"])
     ck, cv = append_kv_cache(t["ds_k0"], t["ds_v0"], t["ds_nk"], t["ds_nv"])
     assert torch.equal(ck, t["cat_k"]) and torch.equal(cv, t["cat_v"])
+
+
+@pytest.mark.parametrize("value,kernel", [(None, False), ("1", True), ("0", False), ("", False),
+                                          ("true", False), ("yes", False)])
+def test_cuda_append_opt_in_follows_the_reference(value, kernel, monkeypatch):
+    """KOTFLASH_ENABLE_CUDA_APPEND keeps the reference's meaning
+    (kotflash/cache.py:163-168, :248): only "1" lets append(backend="auto")
+    use the append kernel, and the same value turns the fused auto route of
+    append_and_attend off."""
+    from kotflash_b200.cache import cuda_append_opted_in, fused_append_auto_allowed
+
+    if value is None:
+        monkeypatch.delenv("KOTFLASH_ENABLE_CUDA_APPEND", raising=False)
+    else:
+        monkeypatch.setenv("KOTFLASH_ENABLE_CUDA_APPEND", value)
+    assert cuda_append_opted_in() is kernel
+    assert fused_append_auto_allowed() is (not kernel)
+    assert cuda_append_opted_in(env=value) is kernel
+
+
+def test_auto_append_on_cpu_stays_on_torch_copies_with_the_opt_in(monkeypatch):
+    monkeypatch.setenv("KOTFLASH_ENABLE_CUDA_APPEND", "1")
+    cache = PreallocatedKVCache(1, 2, 8, 4, device="cpu", dtype=torch.float16)
+    k = torch.randn(1, 2, 3, 4).half()
+    cache.append(k, -k)  # CPU tensors never reach the kernel
+    assert torch.equal(cache.k[:, :, :3], k) and cache.length == 3

@@ -90,3 +90,27 @@ def test_backward_prefill_config_full_size(dtype):
 def test_backward_odd_head_dim_config(d, causal):
     """BASELINE cfg5 geometry (B2 Hq16 Hkv4 D72/96 fp16) at S=2048 (oracle cost)."""
     _run(2, 16, 4, 2048, 2048, d, causal, torch.float16, seed=5)
+
+
+@pytest.mark.parametrize("d", [72, 96])
+@pytest.mark.parametrize("causal", [False, True])
+def test_backward_odd_head_dim_full_length_unit(d, causal):
+    """BASELINE cfg5 at its full length S=16384 (fp16, D72/96), one (batch,
+    KV-head) unit: 4 query heads over one KV head, the unit each of the 8
+    ranks owns when cfg5 is sharded.  The oracle runs chunked over query rows
+    on the GPU in fp32."""
+    s = 16384
+    q = _rand((1, 4, s, d), torch.float16, 50 + d)
+    k = _rand((1, 1, s, d), torch.float16, 51 + d)
+    v = _rand((1, 1, s, d), torch.float16, 52 + d)
+    do = _rand((1, 4, s, d), torch.float16, 53 + d)
+    scale = d ** -0.5
+    out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
+    dq, dk, dv = attention_backward(q, k, v, out, lse, do, causal=causal, scale=scale)
+    eo, el, edq, edk, edv = oracle.forward_backward_chunked(q, k, v, do, causal=causal, scale=scale)
+    tag = f"cfg5 S16384 D{d} causal={causal}"
+    check_close(out, eo, name=f"{tag} O")
+    check_close(lse, el, name=f"{tag} LSE")
+    check_close(dq, edq, name=f"{tag} dQ")
+    check_close(dk, edk, name=f"{tag} dK")
+    check_close(dv, edv, name=f"{tag} dV")

@@ -83,3 +83,18 @@ def test_oracle_append_matches_reference_cache_sequence():
     torch.testing.assert_close(cache[:, :, :8], z["kview"], rtol=0, atol=0)
     o, _ = oracle.forward(z["q"], z["kview"], z["vview"], causal=False)
     torch.testing.assert_close(o, z["attend"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_chunked_oracle_equals_the_full_one(causal):
+    """forward_backward_chunked (used at the 16384-token length) computes the
+    same fp32 results as forward_backward, chunk by chunk."""
+    g = torch.Generator().manual_seed(9)
+    q = torch.randn(2, 4, 70, 24, generator=g)
+    k = torch.randn(2, 2, 90, 24, generator=g)
+    v = torch.randn(2, 2, 90, 24, generator=g)
+    do = torch.randn(2, 4, 70, 24, generator=g)
+    full = oracle.forward_backward(q, k, v, do, causal=causal)
+    chunked = oracle.forward_backward_chunked(q, k, v, do, causal=causal, chunk=16)
+    for a, b in zip(full, chunked):
+        torch.testing.assert_close(a, b, atol=1e-5, rtol=1e-5)

@@ -78,3 +78,24 @@ def test_decode_noalloc_rejects_splits_beyond_the_static_scratch():
                                _ext.dtype_code(q.dtype), 0.1, 512, _ext.stream_of(q))
     assert rc == _ext.KF_ERR_WORKSPACE
     assert "static maximum" in _ext.last_error()
+
+
+def test_decode_noalloc_lowers_the_planned_split_count_to_fit():
+    """B2 Hq256 Hkv128 Sq16 D128 Sk1024: the planner asks for 2 splits whose
+    partials (2 x 4.2 MB) overflow the 8 MiB array, so the entry point lowers
+    the count to what fits (1 split, written straight to O).  Its result must
+    equal kf_decode's with that one split bit for bit, on two calls in a row."""
+    lib = _ext.load()
+    b, hq, hkv, sq, sk, d = 2, 256, 128, 16, 1024, 128
+    planned = lib.kf_decode_num_splits(b, hq, hkv, sq, sk, d, _ext.sm_count(0))
+    assert planned == 2
+    per_split = b * hq * sq * (d + 1) * 4
+    assert planned * per_split + 256 > 8 << 20  # the plan does not fit the static array
+    q = _rand((b, hq, sq, d), torch.bfloat16, 7)
+    k = _rand((b, hkv, sk, d), torch.bfloat16, 8)
+    v = _rand((b, hkv, sk, d), torch.bfloat16, 9)
+    want_o, want_lse = _with_workspace(lib, q, k, v, 1)
+    for _ in range(2):
+        got_o, got_lse = _no_alloc(lib, q, k, v, 0)
+        torch.cuda.synchronize()
+        assert torch.equal(got_o, want_o) and torch.equal(got_lse, want_lse)
