@@ -1114,7 +1114,7 @@ def main(argv=None) -> int:
                               "tflops": round(world * per_rank / (copy_ms * 1e-3) / 1e12, 2),
                               "agg_gbs": round(world * (h2d + d2h) / (copy_ms * 1e-3) / 1e9, 1),
                               "frac": round(copy_ms / e2e_ms, 3),
-                              "note": "same H2D+D2H copies, no compute, all ranks at once"}}
+                              "note": "the copies alone, all ranks at once"}}
 
     peak = peaks["bf16_tflops"]
     bwd_achieved = f_bwd / (bwd_ms * 1e-3) / 1e12
@@ -1125,7 +1125,7 @@ def main(argv=None) -> int:
         "achieved": round(bwd_achieved, 1), "peak": peak, "unit": "TFLOP/s",
         "frac": round(bwd_achieved / peak, 4),
         "traffic": traffic.get("bwd_main_bytes_per_launch"),
-        "traffic_source": traffic.get("source"),
+        "traffic_source": "ncu, one launch: profiles/traffic.json",
         "peak_source": f"{peaks['source']} (burst bf16 cuBLAS)",
         "forward": {"kernel": "kf_attn_fwd", "achieved": round(fwd_achieved, 1),
                     "frac": round(fwd_achieved / peak, 4),
@@ -1153,8 +1153,8 @@ def main(argv=None) -> int:
         use_all_host_cores()
         tflops, per_unit, dtn, runs, threads = cpu_unit_sample(args.dtype)
         cpu = {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": f"{runs} run(s) of one (batch, kv-head) unit of 32 ({dtn}): reference "
-                         f"backend='sdpa' route + autograd, {per_unit:.2f} s/unit"}
+               "sample": f"{runs} x 1 (batch, kv-head) unit of 32 ({dtn}), backend='sdpa' + autograd, "
+                         f"{per_unit:.2f} s/unit"}
 
     if rank == 0:
         if decode is not None:
@@ -1192,8 +1192,12 @@ def main(argv=None) -> int:
             "frac_of_peak": round(value / world / peak, 4),
             "roofline": roofline, "clocks": clocks,
             "gpu_launches": 4 * args.steps,
-            "parity": parity, "fp16": fp16, "cfg5": cfg5, "decode": dec,
-            "decode_multi_gpu": multi, "e2e": e2e, "cpu_baseline": cpu,
+            "e2e": e2e, "cpu_baseline": cpu,
+            # extras: the end of the line is what a 1500-character tail keeps
+            "decode_multi_gpu": multi, "cfg5": cfg5, "fp16": fp16,
+            "fwd": {"tflops": round(fwd_achieved, 1), "frac": round(fwd_achieved / peak, 4),
+                    "bwd_tflops": round(bwd_achieved, 1), "bwd_frac": round(bwd_achieved / peak, 4)},
+            "decode": dec, "parity": parity,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -59,6 +59,14 @@ constexpr int kBM = 64;    // query rows per step
 constexpr int kBN = 128;   // keys per CTA
 constexpr int kStages = 3;  // Q/dO/statistics ring
 constexpr int kThreads = 480;  // 15 warps
+// (batch, KV head) pairs per launch group of the main kernel: with 8 the
+// greedy block scheduler ends the grid as evenly as the global
+// heaviest-first order does (a simulation of the causal 4096-token config
+// over 148 SMs: 928 step-times either way, 968 with 4 pairs, 1056 with 1).
+#ifndef KF_BWD_PAIRS_PER_GROUP
+#define KF_BWD_PAIRS_PER_GROUP 8
+#endif
+constexpr int kPairsPerGroup = KF_BWD_PAIRS_PER_GROUP;
 // TMEM columns
 constexpr uint32_t kColDV = 0, kColDK = 128, kColS = 256, kColDP = 384;
 // 16-bit P^T / dS^T of query columns [32 wg, 32 wg + 32) are packed into the
@@ -80,6 +88,7 @@ struct BwdParams {
   const float* lse2;      // [B*Hq][Sq_pad] LSE * log2(e); +inf on padded rows
   const float* delta;     // [B*Hq][Sq_pad]
   int B, Hq, Hkv, G, Sq, Sk, D, Sq_pad, nqb, nkb;
+  int pairs_per_group;    // (batch, KV head) pairs whose CTAs are launched together
   int causal;
   float scale_log2, scale;
   int32_t* status;
@@ -142,10 +151,21 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(sLD + kStages * 2 * kBM);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Heaviest first: every CTA of key block 0 (the most causal work) launches
-  // before any of key block 1, and so on, so the grid ends on light CTAs.
-  const int bkv = blockIdx.x % (p.B * p.Hkv);
-  const int n = blockIdx.x / (p.B * p.Hkv);
+  // CTA order: the (batch, KV head) pairs go in groups of pairs_per_group;
+  // inside a group every CTA of key block 0 (the most causal work) launches
+  // before any of key block 1, and so on, so each group (and the grid) ends
+  // on light CTAs.  Every CTA walks its query blocks from the last one down,
+  // one block at a time over the group's heads, so the CTAs of one pair,
+  // launched together, add into the same dQ accumulator tiles and read the
+  // same Q/dO tiles at about the same time: each tile passes through DRAM
+  // about once instead of once per wave of key blocks.
+  const int n_pairs = p.B * p.Hkv;
+  const int per_group = p.pairs_per_group * p.nkb;
+  const int grp = (int)blockIdx.x / per_group;
+  const int rem = (int)blockIdx.x - grp * per_group;
+  const int gp = min(p.pairs_per_group, n_pairs - grp * p.pairs_per_group);
+  const int n = rem / gp;
+  const int bkv = grp * p.pairs_per_group + rem % gp;
   const int b = bkv / p.Hkv, kvh = bkv % p.Hkv;
   const int i0 = p.causal ? min((n * kBN) / kBM, p.nqb) : 0;
   const int nq_steps = p.nqb - i0;
@@ -180,9 +200,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   kf::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
+  // step s: query block nqb - 1 - s / G (last block first), head s % G of the group
   auto step_coords = [&](int s, int& h, int& i) {
-    h = kvh * p.G + s / nq_steps;
-    i = i0 + s % nq_steps;
+    h = kvh * p.G + s % p.G;
+    i = p.nqb - 1 - s / p.G;
   };
 
   if (warp == 12) {
@@ -292,8 +313,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int key = n * kBN + kr;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
-    int i_step = i0;  // query block of step s (steps walk heads, then blocks i0..nqb-1)
-    for (int s = 0; ok && s < nsteps; ++s, i_step = (i_step + 1 == p.nqb) ? i0 : i_step + 1) {
+    for (int s = 0; ok && s < nsteps; ++s) {
+      const int i_step = p.nqb - 1 - s / p.G;  // query block of step s (see step_coords)
       const int st = s % kStages, buf = s & 1;
       if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
       // The row statistics are read into registers before waiting for S^T:
@@ -669,6 +690,7 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   p.Sq_pad = Sq_pad;
   p.nqb = nqb;
   p.nkb = nkb;
+  p.pairs_per_group = kPairsPerGroup;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * kLog2e;
   p.scale = scale;
