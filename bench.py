@@ -781,42 +781,50 @@ class DecoderBlock(torch.nn.Module):
         return x + self.w_down(F.silu(self.w_gate(y)) * self.w_up(y))
 
 
-def decoder_block_step(model, opt, x, target, backend):
+def decoder_block_step(model, opt, x, target, backend, attn_dtype=torch.float16):
     import torch.nn.functional as F
 
     opt.zero_grad(set_to_none=True)
-    loss = F.mse_loss(model(x, backend), target)
+    loss = F.mse_loss(model(x, backend, attn_dtype), target)
     loss.backward()
     opt.step()
     return loss.detach()
 
 
-def bench_decoder_block(batch=2, seq=4096, q_heads=32, kv_heads=8, head_dim=128, warmup=3, iters=5):
+def bench_decoder_block(batch=2, seq=4096, q_heads=32, kv_heads=8, head_dim=128, warmup=3, iters=5,
+                        bf16_block=False):
     """Training step (forward, backward, AdamW) of the decoder block per
     attention backend, same initial weights and inputs; tokens/s from the
-    median CUDA-event step time.  fp32 projections (no TF32), fp16 attention,
-    as the reference benchmark runs it."""
+    median CUDA-event step time.  Default: fp32 projections (no TF32), fp16
+    attention, as the reference benchmark runs it; there the fp32
+    projections take nearly all of the step.  ``bf16_block``: the whole block
+    (parameters, projections, attention) in bf16, so the attention's share
+    of the step shows."""
     torch.manual_seed(1234)
     hidden = q_heads * head_dim
-    x = torch.randn(batch, seq, hidden, device="cuda")
+    pdt = torch.bfloat16 if bf16_block else torch.float32
+    adt = torch.bfloat16 if bf16_block else torch.float16
+    x = torch.randn(batch, seq, hidden, device="cuda").to(pdt)
     target = torch.randn_like(x)
     init = {k: v.detach().clone() for k, v in DecoderBlock(q_heads, kv_heads, head_dim).state_dict().items()}
     out = {"shape": {"batch": batch, "seq": seq, "q_heads": q_heads, "kv_heads": kv_heads, "head_dim": head_dim,
                      "hidden": hidden},
-           "precision": "fp32 parameters and projections (TF32 off), fp16 attention, AdamW"}
+           "precision": ("bf16 parameters, projections and attention, AdamW" if bf16_block else
+                         "fp32 parameters and projections (TF32 off), fp16 attention, AdamW")}
     for backend in ("kotflash_b200", "sdpa_gqa", "sdpa_expanded_kv"):
         try:
             model = DecoderBlock(q_heads, kv_heads, head_dim).cuda()
             model.load_state_dict(init)
+            model = model.to(pdt)
             opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
             for _ in range(warmup):
-                decoder_block_step(model, opt, x, target, backend)
+                decoder_block_step(model, opt, x, target, backend, adt)
             torch.cuda.synchronize()
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
             loss = None
             for a, e in evs:
                 a.record()
-                loss = decoder_block_step(model, opt, x, target, backend)
+                loss = decoder_block_step(model, opt, x, target, backend, adt)
                 e.record()
             torch.cuda.synchronize()
             ms = statistics.median(a.elapsed_time(e) for a, e in evs)
@@ -1146,7 +1154,8 @@ def main(argv=None) -> int:
             decode = {"sweep": bench_decode_sweep(peaks), "kv_cache_loop": bench_cache_loop(peaks)}
     comparators = (bench_sdpa_comparators(dtype)
                    if (rank == 0 and world == 1 and not args.no_comparators) else None)
-    block = bench_decoder_block() if (rank == 0 and world == 1 and not args.no_comparators) else None
+    block = ({"fp32_projections": bench_decoder_block(), "bf16_block": bench_decoder_block(bf16_block=True)}
+             if (rank == 0 and world == 1 and not args.no_comparators) else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -11,29 +11,41 @@
 // so every K/V tile fetched by TMA feeds both.  Warp roles:
 //   warps 0-3  softmax for tile 0   (thread t owns query row t = TMEM lane t)
 //   warps 4-7  softmax for tile 1
-//   warp  8    TMA producer (Q once, then K/V blocks of 128 keys)
+//   warp  8    TMA producer (Q once, then K/V blocks of BN keys)
 //   warp  9    TMEM allocator + tcgen05.mma issuer for tile 0
 //   warp 10    tcgen05.mma issuer for tile 1
 //   warp 11    spare (completes the third warpgroup)
 // The softmax warpgroups raise their register limit to 224 (setmaxnreg) and
-// warps 8-11 lower theirs to 56, which removes most softmax spills (+2%).
-// Tensor memory (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
-// P (16-bit) overwrites the first 64 columns of its S tile and feeds the
-// PV product directly from TMEM (A operand in tensor memory).
-// Each tile's issuer runs, per KV block j,
-//   O_t += P_t,j V_j ; S_t = Q_t K_{j+1}^T
-// so one tile's softmax overlaps the other tile's two GEMMs.  Two issuing
-// threads matter on sm_100: the tensor pipe holds almost no queued MMAs, so
-// every cycle an issuing thread spends on an mbarrier wait, a tcgen05 fence
-// or a commit would idle the pipe; with one issuer per tile, the other tile's
-// MMAs fill those gaps.  A tile's "S ready" commit also covers its previous
-// PV, which makes O safe to rescale when the softmax sees the next S.  The
-// running max is only raised (and O rescaled) when it grows by more than 2^8,
-// so most blocks skip the O round trip; P stays <= 256, which fp16/bf16 hold
-// exactly enough.  The softmax computes its exponentials partly on the MUFU
-// unit and partly as a polynomial on the fp32 pipe (packed f32x2 arithmetic),
-// because 16 MUFU results per clock per SM alone cannot keep up with the
-// tensor cores at head_dim 128.
+// warps 8-11 lower theirs to 56.
+//
+// Each tile has its own score buffer S, probability buffer P (16-bit) and
+// output accumulator O in tensor memory (512 columns):
+//   BN = 80 keys per block (head_dim > 64):
+//     S0 [0,80) P0 [80,120) S1 [128,208) P1 [208,248) O0 [256,384) O1 [384,512)
+//   BN = 128 keys per block (head_dim <= 64):
+//     S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384) P0 [384,448) P1 [448,512)
+// Because P does not overlay S, a tile's softmax releases S as soon as it has
+// loaded the scores into registers, and the tile's issuer computes the next
+// block's S = Q K^T while the softmax still works on this block; P feeds the
+// O += P V product straight from tensor memory (A operand in TMEM).  Per tile
+// and block j the issuer runs
+//   [S(j) loaded]  S(j+1) = Q K_{j+1}^T      [P(j) stored]  O += P(j) V_j
+// so the softmax of a tile runs block after block without waiting for its own
+// GEMMs, and the two tiles' GEMMs fill the tensor pipe between them.  With
+// P over S (an earlier layout) each tile's chain was softmax + its two GEMMs
+// in series, and the tensor pipe sat idle about half the time.  80 keys is the
+// widest block whose S and P fit beside a 128-column O (2 x (80 + 40 + 128)
+// <= 512); Q K^T with N = 80 costs a little shared-memory bandwidth per FLOP.
+// Two issuing threads matter on sm_100: the tensor pipe holds almost no
+// queued MMAs, so every cycle an issuing thread spends on an mbarrier wait, a
+// tcgen05 fence or a commit would idle the pipe; with one issuer per tile,
+// the other tile's MMAs fill those gaps.  The running max is only raised (and
+// O rescaled) when it grows by more than 2^8, so most blocks skip the O round
+// trip; P stays <= 256, which fp16/bf16 hold exactly enough.  The softmax
+// computes its exponentials partly on the MUFU unit and partly as a
+// polynomial on the fp32 pipe (packed f32x2 arithmetic), because 16 MUFU
+// results per clock per SM alone cannot keep up with the tensor cores at
+// head_dim 128.
 #include <math.h>
 
 #include <algorithm>
@@ -44,19 +56,23 @@
 namespace {
 
 constexpr int kBlockM = 128;
-constexpr int kBlockN = 128;
 constexpr int kThreads = 384;  // 3 warpgroups: two softmax, one producer + MMA issuers + spare
 // Register split between the warpgroups (setmaxnreg): a softmax thread holds a
 // 128-column score row and its packed probabilities, the other roles little.
 // 256 * 224 + 128 * 56 = 384 * 168, the allocation the block launches with.
 constexpr int kRegSoftmax = 224, kRegOther = 56;
-constexpr int kStages = 2;
+constexpr int kMaxStages = 4;  // deepest K/V ring (kv_stages)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Of every 8 exponential pairs in an unmasked block, this many run as the
 // fp32-pipe polynomial and the rest on MUFU.
-constexpr int kPolyPairs = 2;
+// (1 and 3 of 8 measured no faster with the early-release schedule)
+#ifndef KF_FWD_POLY_PAIRS
+#define KF_FWD_POLY_PAIRS 2
+#endif
+constexpr int kPolyPairs = KF_FWD_POLY_PAIRS;
+
 
 struct FwdParams {
   uint16_t* o;
@@ -72,11 +88,21 @@ struct FwdParams {
   int32_t* status;
 };
 
+// Keys per K/V block and K/V ring depth for a head dim of KS * 16: 80-key
+// blocks when O needs 128 TMEM columns, 128 otherwise (layouts above).
+__host__ __device__ constexpr int block_n(int ks) { return ks > 4 ? 80 : 128; }
+__host__ __device__ constexpr int kv_stages(int ks) { return ks > 4 ? 3 : 4; }
+__host__ __device__ constexpr uint32_t s_col_of(int bn, int t) { return (uint32_t)(t * 128 + 0 * bn); }
+__host__ __device__ constexpr uint32_t p_col_of(int bn, int t) {
+  return bn == 128 ? 384u + 64u * t : (uint32_t)(t * 128 + bn);
+}
+__host__ __device__ constexpr uint32_t o_col_of(int bn, int t) { return bn == 128 ? 256u + 64u * t : 256u + 128u * t; }
+
 struct __align__(8) FwdBarriers {
   uint64_t q_full, q_empty;
-  uint64_t k_full[kStages], k_empty[kStages];
-  uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], p_full[2];
+  uint64_t k_full[kMaxStages], k_empty[kMaxStages];
+  uint64_t v_full[kMaxStages], v_empty[kMaxStages];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
   uint64_t o_final[2];
   uint64_t turn[2];  // exponential phases of the two tiles alternate
   uint32_t tmem_base;
@@ -114,6 +140,7 @@ struct TileInfo {
 // of gridDim.x items, in forward order on even rounds and reverse order on
 // odd rounds, so a CTA that drew a heavy item in one round draws a light one
 // in the next and the CTAs' totals stay close.
+template <int BN>
 __device__ __forceinline__ TileInfo tile_info(const FwdParams& p, int item) {
   TileInfo ti;
   const int per_bh = p.ctas_per_kvh;
@@ -134,7 +161,7 @@ __device__ __forceinline__ TileInfo tile_info(const FwdParams& p, int item) {
     if (ti.valid[t]) row_end_max = max(row_end_max, min(ti.row0[t] + kBlockM, p.Sq));
   }
   const int key_end = p.causal ? min(p.Sk, row_end_max) : p.Sk;
-  ti.n_blocks = (key_end + kBlockN - 1) / kBlockN;
+  ti.n_blocks = (key_end + BN - 1) / BN;
   return ti;
 }
 
@@ -149,15 +176,19 @@ template <bool BF16, int NP, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const FwdParams p) {
-  constexpr int PANEL = kBlockM * 128;      // bytes of one 64-column panel of 128 rows
-  constexpr int TILE = NP * PANEL;          // one 128-row tile, all panels
+  constexpr int BN = block_n(KS);             // keys per K/V block
+  constexpr int STAGES = kv_stages(KS);       // K/V ring depth
+  constexpr int QPANEL = kBlockM * 128;       // bytes of one 64-column panel of a 128-row Q tile
+  constexpr int QTILE = NP * QPANEL;
+  constexpr int KPANEL = BN * 128;            // one 64-column panel of a K or V block
+  constexpr int KTILE = NP * KPANEL;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sQ = smem;                          // [2][NP][128][64]
-  uint8_t* sK = sQ + 2 * TILE;                 // [kStages][NP][128][64]
-  uint8_t* sV = sK + kStages * TILE;           // [kStages][NP][128][64]
-  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(sV + kStages * TILE);
+  uint8_t* sK = sQ + 2 * QTILE;                // [STAGES][NP][BN][64]
+  uint8_t* sV = sK + STAGES * KTILE;           // [STAGES][NP][BN][64]
+  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(sV + STAGES * KTILE);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
@@ -165,7 +196,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   if (tid == 0) {
     kf::mbar_init(&bars->q_full, 1);
     kf::mbar_init(&bars->q_empty, 2);  // one commit per issuer
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       kf::mbar_init(&bars->k_full[s], 1);
       kf::mbar_init(&bars->k_empty[s], 2);
       kf::mbar_init(&bars->v_full[s], 1);
@@ -173,7 +204,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     }
     for (int t = 0; t < 2; ++t) {
       kf::mbar_init(&bars->s_full[t], 1);
+      kf::mbar_init(&bars->s_free[t], 128);
       kf::mbar_init(&bars->p_full[t], 128);
+      kf::mbar_init(&bars->pv_done[t], 1);
       kf::mbar_init(&bars->o_final[t], 1);
       kf::mbar_init(&bars->turn[t], 128);
     }
@@ -196,7 +229,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
 
   // Persistent CTA: every role walks the same item sequence (round_item);
   // barrier phases run on across items (g counts K/V blocks of all items,
-  // it counts items).
+  // it counts items, jt counts a tile's blocks).
   const int rounds = (p.n_items + (int)gridDim.x - 1) / (int)gridDim.x;
   if (warp >= 8) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegOther));
@@ -207,30 +240,35 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       for (int rd = 0; rd < rounds; ++rd) {
         const int item = round_item(rd, p.n_items);
         if (item < 0) continue;
-        const TileInfo ti = tile_info(p, item);
+        const TileInfo ti = tile_info<BN>(p, item);
         const int nt = ti.valid[1] ? 2 : 1;
         // the previous item's last QK^T has read the Q tiles
         if (it > 0 && !wait_bar(&bars->q_empty, (it - 1) & 1, bars, p.status)) break;
-        kf::mbar_arrive_expect_tx(&bars->q_full, nt * TILE);
-        for (int t = 0; t < nt; ++t)
-          for (int pn = 0; pn < NP; ++pn)
-            kf::tma_load_4d(sQ + t * TILE + pn * PANEL, &map_q, &bars->q_full, pn * 64, ti.row0[t],
-                            ti.head[t], ti.b);
+        kf::mbar_arrive_expect_tx(&bars->q_full, nt * QTILE);
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+          if (t < nt)
+#pragma unroll
+            for (int pn = 0; pn < NP; ++pn)
+              kf::tma_load_4d(sQ + t * QTILE + pn * QPANEL, &map_q, &bars->q_full, pn * 64, ti.row0[t],
+                              ti.head[t], ti.b);
         bool ok = true;
         for (int j = 0; j < ti.n_blocks; ++j) {
           const int gj = g + j;
-          const int s = gj % kStages;
-          const uint32_t ph = ((gj / kStages) & 1) ^ 1;
+          const int s = gj % STAGES;
+          const uint32_t ph = ((gj / STAGES) & 1) ^ 1;
           if (!(ok = wait_bar(&bars->k_empty[s], ph, bars, p.status))) break;
-          kf::mbar_arrive_expect_tx(&bars->k_full[s], TILE);
+          kf::mbar_arrive_expect_tx(&bars->k_full[s], KTILE);
+#pragma unroll
           for (int pn = 0; pn < NP; ++pn)
-            kf::tma_load_4d(sK + s * TILE + pn * PANEL, &map_k, &bars->k_full[s], pn * 64,
-                            j * kBlockN, ti.kvh, ti.b);
+            kf::tma_load_4d(sK + s * KTILE + pn * KPANEL, &map_k, &bars->k_full[s], pn * 64, j * BN, ti.kvh,
+                            ti.b);
           if (!(ok = wait_bar(&bars->v_empty[s], ph, bars, p.status))) break;
-          kf::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
+          kf::mbar_arrive_expect_tx(&bars->v_full[s], KTILE);
+#pragma unroll
           for (int pn = 0; pn < NP; ++pn)
-            kf::tma_load_4d(sV + s * TILE + pn * PANEL, &map_v, &bars->v_full[s], pn * 64,
-                            j * kBlockN, ti.kvh, ti.b);
+            kf::tma_load_4d(sV + s * KTILE + pn * KPANEL, &map_v, &bars->v_full[s], pn * 64, j * BN, ti.kvh,
+                            ti.b);
         }
         if (!ok) break;
         g += ti.n_blocks;
@@ -241,28 +279,27 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     // ------------------------------------------------------------ MMA issuers
     const int t = warp - 9;  // this thread issues every MMA of Q tile t
     if (lane == 0) {
-      const uint32_t idesc_qk = kf::make_idesc_f16(BF16, kBlockM, kBlockN, 0, 0);
+      const uint32_t idesc_qk = kf::make_idesc_f16(BF16, kBlockM, BN, 0, 0);
       const uint32_t idesc_pv = kf::make_idesc_f16(BF16, kBlockM, d_pad16, 0, 1);
       // Descriptors are built once; each MMA only adds a compile-time offset
       // to the low word of a base descriptor.
-      const kf::SDesc dq = kf::make_sdesc_split(kf::smem_u32(sQ + t * TILE), 16, 1024);
+      const kf::SDesc dq = kf::make_sdesc_split(kf::smem_u32(sQ + t * QTILE), 16, 1024);
       const kf::SDesc dk = kf::make_sdesc_split(kf::smem_u32(sK), 16, 1024);
-      const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), PANEL, 1024);
-      const uint32_t s_tm = tmem + t * 128, o_tm = tmem + 256 + t * 128;
+      const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), KPANEL, 1024);
+      const uint32_t s_tm = tmem + s_col_of(BN, t), p_tm = tmem + p_col_of(BN, t), o_tm = tmem + o_col_of(BN, t);
       // Each GEMM is one straight-line run of MMAs (compile-time trip counts).
       auto issue_qk = [&](int gj) {
-        const uint32_t koff = (gj % kStages) * TILE;
+        const uint32_t koff = (gj % STAGES) * KTILE;
 #pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-          const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
-          kf::umma_ss(s_tm, kf::sdesc_at(dq, off), kf::sdesc_at(dk, koff + off), idesc_qk, kk > 0);
-        }
+        for (int kk = 0; kk < KS; ++kk)
+          kf::umma_ss(s_tm, kf::sdesc_at_here(dq, (kk >> 2) * QPANEL + (kk & 3) * 32),
+                      kf::sdesc_at_here(dk, koff + (kk >> 2) * KPANEL + (kk & 3) * 32), idesc_qk, kk > 0);
       };
       auto issue_pv = [&](int gj, bool first) {
-        const uint32_t voff = (gj % kStages) * TILE;
+        const uint32_t voff = (gj % STAGES) * KTILE;
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk)
-          kf::umma_ts(o_tm, s_tm + kk * 8, kf::sdesc_at(dv, voff + kk * 2048), idesc_pv,
+        for (int kk = 0; kk < BN / 16; ++kk)
+          kf::umma_ts(o_tm, p_tm + kk * 8, kf::sdesc_at_here(dv, voff + kk * 2048), idesc_pv,
                       (!first || kk > 0));
       };
       int g = 0, it = 0, jt = 0;  // K/V blocks (all items), items, blocks of tile t
@@ -270,7 +307,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       for (int rd = 0; ok && rd < rounds; ++rd) {
         const int item = round_item(rd, p.n_items);
         if (item < 0) continue;
-        const TileInfo ti = tile_info(p, item);
+        const TileInfo ti = tile_info<BN>(p, item);
         const int nt = ti.valid[1] ? 2 : 1;
         const int nblk = ti.n_blocks;
         if (t < nt) {
@@ -281,36 +318,33 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
             for (int k = 0; k < rel; ++k) kf::umma_commit(bar);
           };
           ok = wait_bar(&bars->q_full, it & 1, bars, p.status) &&
-               wait_bar(&bars->k_full[g % kStages], (g / kStages) & 1, bars, p.status);
+               wait_bar(&bars->k_full[g % STAGES], (g / STAGES) & 1, bars, p.status);
           if (!ok) break;
           kf::tc_fence_after();
           issue_qk(g);
           kf::umma_commit(&bars->s_full[t]);
           if (nblk == 1) release(&bars->q_empty);
-          release(&bars->k_empty[g % kStages]);
+          release(&bars->k_empty[g % STAGES]);
           for (int j = 0; j < nblk; ++j) {
             const int gj = g + j;
-            const int s = gj % kStages;
-            const uint32_t ph = (gj / kStages) & 1;
-            const bool more = j + 1 < nblk;
-            const int s1 = (gj + 1) % kStages;
-            const uint32_t ph1 = ((gj + 1) / kStages) & 1;
-            if (!(ok = wait_bar(&bars->v_full[s], ph, bars, p.status))) break;
-            if (more && !(ok = wait_bar(&bars->k_full[s1], ph1, bars, p.status))) break;
+            if (j + 1 < nblk) {
+              // S(j) is in the softmax's registers: compute S(j+1) now
+              const int s1 = (gj + 1) % STAGES;
+              if (!(ok = wait_bar(&bars->s_free[t], (jt + j) & 1, bars, p.status))) break;
+              if (!(ok = wait_bar(&bars->k_full[s1], ((gj + 1) / STAGES) & 1, bars, p.status))) break;
+              kf::tc_fence_after();
+              issue_qk(gj + 1);
+              kf::umma_commit(&bars->s_full[t]);
+              if (j + 2 == nblk) release(&bars->q_empty);  // last QK^T of the item
+              release(&bars->k_empty[s1]);
+            }
+            const int s = gj % STAGES;
+            if (!(ok = wait_bar(&bars->v_full[s], (gj / STAGES) & 1, bars, p.status))) break;
             if (!(ok = wait_bar(&bars->p_full[t], (jt + j) & 1, bars, p.status))) break;
             kf::tc_fence_after();
             issue_pv(gj, j == 0);
-            // PV and the next QK^T go out back to back (a commit between them
-            // would leave the tensor pipe, which queues almost nothing, idle).
-            if (more) {
-              issue_qk(gj + 1);
-              kf::umma_commit(&bars->s_full[t]);
-              release(&bars->v_empty[s]);
-              if (j + 2 == nblk) release(&bars->q_empty);  // last QK^T of the item
-              release(&bars->k_empty[s1]);
-            } else {
-              release(&bars->v_empty[s]);
-            }
+            kf::umma_commit(&bars->pv_done[t]);
+            release(&bars->v_empty[s]);
           }
           kf::umma_commit(&bars->o_final[t]);
           jt += nblk;
@@ -327,33 +361,45 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int t = warp >> 2;        // tile handled by this warpgroup
     const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t s_col = t * 128, o_col = 256 + t * 128;
+    const uint32_t s_col = s_col_of(BN, t), p_col = p_col_of(BN, t), o_col = o_col_of(BN, t);
     int jt = 0, vt = 0, jturn = 0;  // blocks of tile t, items of tile t, blocks of two-tile items
     bool ok = true;
     for (int rd = 0; ok && rd < rounds; ++rd) {
       const int item = round_item(rd, p.n_items);
       if (item < 0) continue;
-      const TileInfo ti = tile_info(p, item);
+      const TileInfo ti = tile_info<BN>(p, item);
       const int nt = ti.valid[1] ? 2 : 1;
       const int nblk = ti.n_blocks;
-      if (!ti.valid[t]) continue;
-      const int row = ti.row0[t] + r;
+      // this warpgroup's tile, selected without indexing the arrays by a
+      // run-time value (which would put TileInfo in local memory)
+      const bool my_valid = t ? ti.valid[1] : ti.valid[0];
+      const int my_row0 = t ? ti.row0[1] : ti.row0[0];
+      const int my_head = t ? ti.head[1] : ti.head[0];
+      if (!my_valid) continue;
+      const int row = my_row0 + r;
       float m_ref = -INFINITY, l_sum = 0.f;
       for (int j = 0; ok && j < nblk; ++j) {
         if (!(ok = wait_bar(&bars->s_full[t], (jt + j) & 1, bars, p.status))) break;
         kf::tc_fence_after();
-        uint32_t sr[128];
+        uint32_t sr[BN];
         kf::tmem_ld32(lane_base + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
         kf::tmem_ld32(lane_base + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-        kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-        kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        if constexpr (BN == 128) {
+          kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+          kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        } else {
+          kf::tmem_ld16(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[16]>(&sr[64]));
+        }
         kf::tmem_wait_ld();
-        const int key0 = j * kBlockN;
-        const bool need_mask = (key0 + kBlockN > p.Sk) || (p.causal && key0 + kBlockN - 1 > ti.row0[t]);
+        // the scores are in registers: the issuer may overwrite S with the next block's
+        kf::tc_fence_before();
+        kf::mbar_arrive(&bars->s_free[t]);
+        const int key0 = j * BN;
+        const bool need_mask = (key0 + BN > p.Sk) || (p.causal && key0 + BN - 1 > my_row0);
         if (need_mask) {
-          const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : kBlockN);
+          const int lim = min(p.Sk - key0, p.causal ? row - key0 + 1 : BN);
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < BN; ++c)
             if (c >= lim) sr[c] = 0xFF800000u;  // -inf
         }
         // Row max of the raw scores (the scale is positive, so it commutes),
@@ -362,7 +408,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         {
           float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 128; c += 8) {
+          for (int c = 0; c < BN; c += 8) {
             a0 = kf::fmax3(a0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
             a1 = kf::fmax3(a1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
             a2 = kf::fmax3(a2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
@@ -391,11 +437,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         // masked blocks (-inf entries) use MUFU only, full blocks send
         // kPolyPairs of every 8 pairs to the fp32-pipe polynomial.
         const uint64_t scl = kf::f2(p.scale_log2, p.scale_log2), negm = kf::f2(-m_use, -m_use);
-        uint32_t pk[64];
+        uint32_t pk[BN / 2];
         uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
         if (need_mask) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
+          for (int c = 0; c < BN / 2; ++c) {
             float x0, x1;
             kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
             const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
@@ -404,7 +450,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
+          for (int c = 0; c < BN / 2; ++c) {
             float x0, x1;
             kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
             const uint64_t pp = (c & 7) < kPolyPairs ? kf::exp2_poly2(x0, x1) : kf::f2(kf::ex2(x0), kf::ex2(x1));
@@ -420,8 +466,18 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
           l_sum += s0 + s1;
         }
         if (nt == 2) kf::mbar_arrive(&bars->turn[t ^ 1]);
-        kf::tmem_st32(lane_base + s_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-        kf::tmem_st32(lane_base + s_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        // P(j) goes where P(j-1) was and O may be rescaled: both need the
+        // previous block's O += P V to have completed
+        if (j > 0) {
+          if (!(ok = wait_bar(&bars->pv_done[t], (jt + j - 1) & 1, bars, p.status))) break;
+          kf::tc_fence_after();
+        }
+        kf::tmem_st32(lane_base + p_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+        if constexpr (BN == 128) {
+          kf::tmem_st32(lane_base + p_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        } else {
+          kf::tmem_st8(lane_base + p_col + 32, *reinterpret_cast<const uint32_t(*)[8]>(&pk[32]));
+        }
         if (__any_sync(0xffffffffu, rescale_o)) {
           // O row *= alpha (alpha == 1 on rows that keep their reference max)
           for (int c0 = 0; c0 < d_pad16; c0 += 32) {
@@ -444,7 +500,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         kf::tc_fence_after();
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
         const bool row_ok = row < p.Sq;
-        uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)ti.head[t] * p.os[1] + (int64_t)row * p.os[2];
+        uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)my_head * p.os[1] + (int64_t)row * p.os[2];
         for (int c0 = 0; c0 < d_pad16; c0 += 32) {
           uint32_t ov[32];
           kf::tmem_ld32(lane_base + o_col + c0, ov);
@@ -463,7 +519,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
           }
         }
         if (row_ok)
-          p.lse[((int64_t)ti.b * p.Hq + ti.head[t]) * p.Sq + row] =
+          p.lse[((int64_t)ti.b * p.Hq + my_head) * p.Sq + row] =
               l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;
       }
       jt += nblk;
@@ -491,8 +547,9 @@ template <bool BF16, int KS>
 int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                const FwdParams& p, cudaStream_t st) {
   constexpr int NP = KS > 4 ? 2 : 1;
-  constexpr int TILE = NP * kBlockM * 128;
-  const size_t smem = 1024 + (size_t)(2 + 2 * kStages) * TILE + sizeof(FwdBarriers);
+  constexpr size_t QTILE = (size_t)NP * kBlockM * 128;
+  constexpr size_t KTILE = (size_t)NP * block_n(KS) * 128;
+  const size_t smem = 1024 + 2 * QTILE + 2 * (size_t)kv_stages(KS) * KTILE + sizeof(FwdBarriers);
   auto kern = fwd_kernel<BF16, NP, KS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
@@ -556,8 +613,9 @@ extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = kf::encode_tmap_4d(&mq, q, box_inner, kBlockM))) return rc;
-  if ((rc = kf::encode_tmap_4d(&mk, k, box_inner, kBlockN))) return rc;
-  if ((rc = kf::encode_tmap_4d(&mv, v, box_inner, kBlockN))) return rc;
+  const int bn = block_n((int)((D + 15) / 16));
+  if ((rc = kf::encode_tmap_4d(&mk, k, box_inner, bn))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mv, v, box_inner, bn))) return rc;
 
   FwdParams p;
   p.o = static_cast<uint16_t*>(o->ptr);

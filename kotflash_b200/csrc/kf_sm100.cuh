@@ -321,6 +321,12 @@ KF_DEVI void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
       : "memory");
 }
 
+KF_DEVI void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // ---------------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor (64 bit):
 //   [0,14)  start address >> 4
@@ -356,6 +362,14 @@ KF_DEVI SDesc make_sdesc_split(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_
 KF_DEVI uint64_t sdesc_at(SDesc base, uint32_t bytes) {
   uint64_t d;
   asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(base.lo + (bytes >> 4)), "r"(base.hi));
+  return d;
+}
+// The same, formed where it is used: the compiler may not hoist the 64-bit
+// descriptors of a whole unrolled MMA run into registers, which matters for
+// an issuing thread that runs with few registers.
+KF_DEVI uint64_t sdesc_at_here(SDesc base, uint32_t bytes) {
+  uint64_t d;
+  asm volatile("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(base.lo + (bytes >> 4)), "r"(base.hi));
   return d;
 }
 
