@@ -1085,11 +1085,16 @@ def main(argv=None) -> int:
     ap.add_argument("--no-parity", action="store_true", help="skip the parity block")
     ap.add_argument("--no-comparators", action="store_true",
                     help="skip timing PyTorch SDPA's own GPU backends and the decoder block")
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="time only the headline prefill step (no fp16, cfg5, parity, decode, e2e, CPU or "
+                         "comparator legs): the short command the ncu captures in profiles/ use")
     ap.add_argument("--decode-case", default=None, metavar="SQ,SK",
                     help="time only the split-KV decode config (B2 Hq8 Hkv2 D64 fp16) at one "
                          "(Sq, Sk) with --warmup/--steps plain launches; prints one JSON line")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
+    if args.only_prefill:
+        args.no_decode = args.no_cpu = args.no_e2e = args.no_parity = args.no_comparators = True
 
     if args.impl == "reference":
         # CPU only: no process group, no GPU; ranks other than 0 exit at once
@@ -1141,8 +1146,8 @@ def main(argv=None) -> int:
         "step_frac": round(value / world / peak, 4),
     }
 
-    fp16 = bench_fp16_prefill(args, world, peaks)
-    odd = bench_odd_head_dim(peaks, world, rank)
+    fp16 = None if args.only_prefill else bench_fp16_prefill(args, world, peaks)
+    odd = [] if args.only_prefill else bench_odd_head_dim(peaks, world, rank)
     parity = bench_parity() if (rank == 0 and not args.no_parity) else None
 
     decode = None
@@ -1168,7 +1173,8 @@ def main(argv=None) -> int:
     if rank == 0:
         if decode is not None:
             detail("decode_sweep", decode["sweep"])
-        detail("odd_head_dim_training", odd)
+        if odd:
+            detail("odd_head_dim_training", odd)
         if comparators is not None:
             detail("gpu_comparators", comparators)
         if block is not None:
@@ -1184,10 +1190,10 @@ def main(argv=None) -> int:
                    "kv_cache_loop": {"us_per_token": loop["us_per_token"], "hbm_frac": loop["hbm_frac"],
                                      "prefill_append_hbm_frac": loop["prefill_append"]["hbm_frac"],
                                      "append_bit_exact": loop["append_bit_exact"]}}
-        cfg5 = {"cols": "d,causal,ms,fwd_bwd_tflops,per_rank_frac",
-                "rows": [[r["d"], int(r["causal"]), r["ms"], r["fwd_bwd_tflops"], r["per_rank_frac"]]
-                         for r in odd],
-                "units_per_rank": odd[0]["units_per_rank"], "scaling": "strong (8 units over the ranks)"}
+        cfg5 = None if not odd else {
+            "cols": "d,causal,ms,fwd_bwd_tflops,per_rank_frac",
+            "rows": [[r["d"], int(r["causal"]), r["ms"], r["fwd_bwd_tflops"], r["per_rank_frac"]] for r in odd],
+            "units_per_rank": odd[0]["units_per_rank"], "scaling": "strong (8 units over the ranks)"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
