@@ -91,6 +91,15 @@ int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
  * GQA group of each KV head.  `workspace` must hold
  * kf_attn_bwd_workspace_bytes(...) bytes (fp32 dQ accumulator + row deltas). */
 size_t kf_attn_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D);
+/* The same plus fp32 dK/dV accumulators.  With a workspace this large a
+ * causal backward whose key blocks give fewer than two CTAs per SM (e.g. one
+ * long-sequence (batch, KV head) unit per GPU) splits each key block's query
+ * range over several CTAs that add their dK/dV parts into the accumulators,
+ * as the reference does with `_attention_bwd_dkv_split` + `_dkv_reduce`
+ * (kotflash/kernels/triton_backward.py:199-332); with the smaller size it
+ * runs one CTA per key block. */
+size_t kf_attn_bwd_workspace_bytes_kv(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk,
+                                      int64_t D);
 int kf_attn_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
                 const kf_tensor4* o, const float* lse, const kf_tensor4* dout,
                 const kf_tensor4* dq, const kf_tensor4* dk, const kf_tensor4* dv,

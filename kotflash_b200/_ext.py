@@ -60,6 +60,7 @@ SIGNATURES = {
     "kf_append": (_I, [_T4, _T4, _T4, _T4, _I64, _I, _VP]),
     "kf_attn_fwd": (_I, [_T4, _T4, _T4, _T4, _VP, _I, _F, _I, _VP, _VP]),
     "kf_attn_bwd_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64]),
+    "kf_attn_bwd_workspace_bytes_kv": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64]),
     "kf_attn_bwd": (_I, [_T4, _T4, _T4, _T4, _VP, _T4, _T4, _T4, _T4, _I, _F, _I, _VP, _SZ,
                          _VP, _VP]),
     "kf_decode_num_splits": (_I, [_I64, _I64, _I64, _I64, _I64, _I64, _I]),

@@ -265,7 +265,7 @@ def attention_backward(q, k, v, out, lse, grad_out, *, causal: bool, scale: floa
     dq = torch.empty((b, hq, sq, d_pad), dtype=q.dtype, device=q.device)
     dk = torch.empty(kp.shape, dtype=k.dtype, device=q.device)
     dv = torch.empty(vp.shape, dtype=v.dtype, device=q.device)
-    ws_bytes = lib.kf_attn_bwd_workspace_bytes(b, hq, sq, d_pad)
+    ws_bytes = lib.kf_attn_bwd_workspace_bytes_kv(b, hq, kp.shape[1], sq, kp.shape[2], d_pad)
     workspace = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
     lse_c = lse.contiguous()
     rc = lib.kf_attn_bwd(

@@ -89,6 +89,12 @@ struct BwdParams {
   const float* delta;     // [B*Hq][Sq_pad]
   int B, Hq, Hkv, G, Sq, Sk, D, Sq_pad, nqb, nkb;
   int pairs_per_group;    // (batch, KV head) pairs whose CTAs are launched together
+  // Query split of a key block over several CTAs (1 = none): key block n's
+  // query blocks are cut into ceil(blocks / part_chunk) near-equal parts,
+  // one CTA each (CTAs whose part does not exist return at once), and every
+  // part adds its fp32 dK/dV into dkv_acc ([B*Hkv*Sk_pad][D] for dK, then
+  // the same for dV) with TMA reduce-add.
+  int parts_max, part_chunk, Sk_pad;
   int causal;
   float scale_log2, scale;
   int32_t* status;
@@ -135,7 +141,8 @@ template <bool BF16, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
-           const __grid_constant__ CUtensorMap map_dq, const BwdParams p) {
+           const __grid_constant__ CUtensorMap map_dq, const __grid_constant__ CUtensorMap map_dk,
+           const __grid_constant__ CUtensorMap map_dv, const BwdParams p) {
   constexpr int KPANEL = kBN * 128;  // 16 KB: 128 rows x 64 columns
   constexpr int QPANEL = kBM * 128;  // 8 KB: 64 rows x 64 columns
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -160,16 +167,25 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   // same Q/dO tiles at about the same time: each tile passes through DRAM
   // about once instead of once per wave of key blocks.
   const int n_pairs = p.B * p.Hkv;
-  const int per_group = p.pairs_per_group * p.nkb;
+  const int per_group = p.pairs_per_group * p.nkb * p.parts_max;
   const int grp = (int)blockIdx.x / per_group;
-  const int rem = (int)blockIdx.x - grp * per_group;
+  int rem = (int)blockIdx.x - grp * per_group;
+  const int part = rem % p.parts_max;
+  rem /= p.parts_max;
   const int gp = min(p.pairs_per_group, n_pairs - grp * p.pairs_per_group);
   const int n = rem / gp;
   const int bkv = grp * p.pairs_per_group + rem % gp;
   const int b = bkv / p.Hkv, kvh = bkv % p.Hkv;
   const int i0 = p.causal ? min((n * kBN) / kBM, p.nqb) : 0;
-  const int nq_steps = p.nqb - i0;
-  const int nsteps = p.G * nq_steps;
+  const int nq_all = p.nqb - i0;  // query blocks that see this key block
+  const bool split = p.parts_max > 1;
+  const int nparts = split ? (nq_all + p.part_chunk - 1) / p.part_chunk : 1;
+  if (split && part >= nparts) return;  // no such part: nothing to do (dK/dV accumulators start at zero)
+  // this CTA's query blocks, in sweep order: [u0, u1) of the nq_all blocks
+  const int u0 = (int)((int64_t)part * nq_all / nparts);
+  const int u1 = (int)((int64_t)(part + 1) * nq_all / nparts);
+  const int s_begin = p.G * u0;         // first (global) step of this CTA
+  const int nsteps = p.G * (u1 - u0);   // loops below count local steps 0 .. nsteps - 1
   constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
 
   if (tid == 0) {
@@ -200,10 +216,12 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   kf::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  // step s: query block nqb - 1 - s / G (last block first), head s % G of the group
+  // local step s = global step s_begin + s: query block nqb - 1 - (global step) / G
+  // (last block first), head (global step) % G of the group
   auto step_coords = [&](int s, int& h, int& i) {
-    h = kvh * p.G + s % p.G;
-    i = p.nqb - 1 - s / p.G;
+    const int gs = s_begin + s;
+    h = kvh * p.G + gs % p.G;
+    i = p.nqb - 1 - gs / p.G;
   };
 
   if (warp == 12) {
@@ -314,7 +332,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
     for (int s = 0; ok && s < nsteps; ++s) {
-      const int i_step = p.nqb - 1 - s / p.G;  // query block of step s (see step_coords)
+      const int i_step = p.nqb - 1 - (s_begin + s) / p.G;  // query block of step s (see step_coords)
       const int st = s % kStages, buf = s & 1;
       if (!(ok = wait_bar(&bars->qdo_full[st], (s / kStages) & 1, bars, p.status))) break;
       // The row statistics are read into registers before waiting for S^T:
@@ -460,7 +478,35 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const float mul = is_dk ? p.scale : 1.f;
     const bool have = nsteps > 0 && wait_bar(&bars->mma_done, 0, bars, p.status);
     if (have) kf::tc_fence_after();
-    if (nsteps == 0 || have) {
+    if (split) {
+      // This CTA's part of dK/dV goes to the fp32 accumulators: each
+      // warpgroup stages its tensor as 128-row x 32-column fp32 boxes
+      // (128-byte swizzle) in shared memory no MMA or TMA load uses any more
+      // (dV over the Q/dO ring, dK over K/V) and one thread adds the boxes
+      // with TMA reduce-add; the finish kernel converts the sums.
+      uint8_t* stage = is_dk ? sK : sQ;
+      if (have) {
+        for (int c0 = 0; c0 < d_pad16; c0 += 32) {
+          uint32_t ov[32];
+          kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0, ov);
+          kf::tmem_wait_ld();
+          uint8_t* row_ptr = stage + (c0 >> 5) * (kBN * 128) + kr * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(row_ptr + ((j ^ (kr & 7)) << 4)) =
+                make_uint4(ov[4 * j], ov[4 * j + 1], ov[4 * j + 2], ov[4 * j + 3]);
+        }
+        kf::fence_proxy_async_smem();
+      }
+      kf::named_bar_sync(is_dk ? 3 : 2, 128);
+      if (have && (warp & 3) == 0 && lane == 0) {
+        const int row0 = bkv * p.Sk_pad + n * kBN;
+        for (int c0 = 0; c0 < d_pad16; c0 += 32)
+          kf::tma_reduce_add_2d(is_dk ? &map_dk : &map_dv, stage + (c0 >> 5) * (kBN * 128), c0, row0);
+        kf::bulk_commit_group();
+        kf::bulk_wait_group<0>();
+      }
+    } else if (nsteps == 0 || have) {
       for (int c0 = 0; c0 < d_pad16; c0 += 32) {
         uint32_t ov[32];
         if (have) {
@@ -505,6 +551,8 @@ struct PrepArgs {
   float* delta;
   float4* acc;         // dQ accumulator, zeroed here
   int64_t acc_vec4;    // its length in float4
+  float4* acc2;        // dK/dV accumulators when key blocks are split (else null), zeroed here
+  int64_t acc2_vec4;
   int64_t os[4], dos[4];
   int Hq, Sq, Sq_pad, D;
   int64_t rows;  // B*Hq*Sq_pad
@@ -543,6 +591,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < a.acc_vec4; i += (int64_t)gridDim.x * 256)
     a.acc[i] = z;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < a.acc2_vec4; i += (int64_t)gridDim.x * 256)
+    a.acc2[i] = z;
 }
 
 // dQ = scale * workspace ([bh][qb][D][64] fp32) -> dq [B,Hq,Sq,D] in the input
@@ -584,6 +634,43 @@ __global__ void __launch_bounds__(256) finish_kernel(const FinishArgs a) {
   }
 }
 
+// dK = scale * acc_k, dV = acc_v ([B*Hkv*Sk_pad][D] fp32 sums of the split
+// parts) -> the caller's dk/dv in the input dtype: eight consecutive columns
+// of one key row per thread, 16-byte stores.
+struct FinishKVArgs {
+  const float* acc_k;
+  const float* acc_v;
+  uint16_t* dk;
+  uint16_t* dv;
+  int64_t dks[4], dvs[4];
+  int Hkv, Sk, Sk_pad, D;
+  float scale;
+  int64_t rows;  // B*Hkv*Sk
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) finish_kv_kernel(const FinishKVArgs a) {
+  const int nd8 = a.D / 8;
+  for (int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x; idx < 2 * a.rows * nd8;
+       idx += (int64_t)gridDim.x * 256) {
+    const bool is_v = idx >= a.rows * nd8;
+    const int64_t li = is_v ? idx - a.rows * nd8 : idx;
+    const int64_t row = li / nd8;
+    const int d8 = (int)(li % nd8) * 8;
+    const int64_t bh = row / a.Sk;
+    const int key = (int)(row % a.Sk);
+    const float* src = (is_v ? a.acc_v : a.acc_k) + (bh * a.Sk_pad + key) * a.D + d8;
+    const float4 x = reinterpret_cast<const float4*>(src)[0], y = reinterpret_cast<const float4*>(src)[1];
+    const float m = is_v ? 1.f : a.scale;
+    const int64_t b = bh / a.Hkv, h = bh % a.Hkv;
+    const int64_t* st = is_v ? a.dvs : a.dks;
+    uint16_t* dst = (is_v ? a.dv : a.dk) + b * st[0] + h * st[1] + (int64_t)key * st[2] + d8;
+    *reinterpret_cast<uint4*>(dst) =
+        make_uint4(kf::pack2<BF16>(x.x * m, x.y * m), kf::pack2<BF16>(x.z * m, x.w * m),
+                   kf::pack2<BF16>(y.x * m, y.y * m), kf::pack2<BF16>(y.z * m, y.w * m));
+  }
+}
+
 bool rows16(const kf_tensor4* t) {
   if (!t || !kf::aligned16(t->ptr) || t->stride[3] != 1) return false;
   for (int i = 0; i < 3; ++i)
@@ -595,44 +682,46 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 template <bool BF16, int KS>
 int launch_bwd_main(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                    const CUtensorMap& mdo, const CUtensorMap& mdq, const BwdParams& p,
-                    cudaStream_t st) {
+                    const CUtensorMap& mdo, const CUtensorMap& mdq, const CUtensorMap& mdk,
+                    const CUtensorMap& mdv, const BwdParams& p, cudaStream_t st) {
   const size_t smem = 1024 + 4 * 128 * 128 + kStages * 4 * kBM * 128 + 2 * 128 * 128 +
                       2 * 128 * 128 + kStages * 2 * kBM * 4 + sizeof(BwdBarriers);
   auto kern = bwd_kernel<BF16, KS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_bwd: cannot reserve %zu bytes of shared memory", smem);
-  const int64_t grid = (int64_t)p.B * p.Hkv * p.nkb;
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, p);
+  const int64_t grid = (int64_t)p.B * p.Hkv * p.nkb * p.parts_max;
+  if (grid > 0x7fffffffLL) return kf::set_error(KF_ERR_UNSUPPORTED, "kf_attn_bwd: grid too large");
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mdo, mdq, mdk, mdv, p);
   return kf::check_launch("kf_attn_bwd main");
 }
 
 template <bool BF16>
 int dispatch_bwd_main(int ks, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                      const CUtensorMap& mdo, const CUtensorMap& mdq, const BwdParams& p,
-                      cudaStream_t st) {
+                      const CUtensorMap& mdo, const CUtensorMap& mdq, const CUtensorMap& mdk,
+                      const CUtensorMap& mdv, const BwdParams& p, cudaStream_t st) {
   switch (ks) {
-    case 1: return launch_bwd_main<BF16, 1>(mq, mk, mv, mdo, mdq, p, st);
-    case 2: return launch_bwd_main<BF16, 2>(mq, mk, mv, mdo, mdq, p, st);
-    case 3: return launch_bwd_main<BF16, 3>(mq, mk, mv, mdo, mdq, p, st);
-    case 4: return launch_bwd_main<BF16, 4>(mq, mk, mv, mdo, mdq, p, st);
-    case 5: return launch_bwd_main<BF16, 5>(mq, mk, mv, mdo, mdq, p, st);
-    case 6: return launch_bwd_main<BF16, 6>(mq, mk, mv, mdo, mdq, p, st);
-    case 7: return launch_bwd_main<BF16, 7>(mq, mk, mv, mdo, mdq, p, st);
-    default: return launch_bwd_main<BF16, 8>(mq, mk, mv, mdo, mdq, p, st);
+    case 1: return launch_bwd_main<BF16, 1>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    case 2: return launch_bwd_main<BF16, 2>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    case 3: return launch_bwd_main<BF16, 3>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    case 4: return launch_bwd_main<BF16, 4>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    case 5: return launch_bwd_main<BF16, 5>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    case 6: return launch_bwd_main<BF16, 6>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    case 7: return launch_bwd_main<BF16, 7>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
+    default: return launch_bwd_main<BF16, 8>(mq, mk, mv, mdo, mdq, mdk, mdv, p, st);
   }
 }
 
 template <bool BF16>
 int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const kf_tensor4* o,
             const float* lse, const kf_tensor4* dout, const kf_tensor4* dq, const kf_tensor4* dk,
-            const kf_tensor4* dv, float scale, int causal, void* workspace, int32_t* status,
-            cudaStream_t st) {
+            const kf_tensor4* dv, float scale, int causal, void* workspace, size_t workspace_bytes,
+            int32_t* status, cudaStream_t st) {
   const int B = (int)q->size[0], Hq = (int)q->size[1], Sq = (int)q->size[2], D = (int)q->size[3];
   const int Hkv = (int)k->size[1], Sk = (int)k->size[2];
   const int Sq_pad = (Sq + kBM - 1) / kBM * kBM;
   const int nqb = Sq_pad / kBM;
   const int nkb = (Sk + kBN - 1) / kBN;
+  const int Sk_pad = nkb * kBN;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
   float* dq_acc = reinterpret_cast<float*>(ws);
@@ -640,6 +729,34 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   float* lse2 = reinterpret_cast<float*>(ws + acc_bytes);
   const size_t row_bytes = align256((size_t)B * Hq * Sq_pad * 4);
   float* delta = reinterpret_cast<float*>(ws + acc_bytes + row_bytes);
+  const size_t kv_acc_bytes = align256((size_t)B * Hkv * Sk_pad * D * 4);
+  float* dk_acc = reinterpret_cast<float*>(ws + acc_bytes + 2 * row_bytes);
+  float* dv_acc = reinterpret_cast<float*>(ws + acc_bytes + 2 * row_bytes + kv_acc_bytes);
+
+  // Query split of the key blocks, for causal problems with fewer key-block
+  // CTAs than two per SM (a long sequence sharded to one (batch, KV head)
+  // unit per GPU: key block 0 sees every query block, the last one almost
+  // none, so one CTA per key block would leave the grid waiting on its
+  // heaviest CTA).  Parts target about two waves of equal CTAs; they need
+  // the dK/dV accumulators, i.e. a workspace of
+  // kf_attn_bwd_workspace_bytes_kv bytes.
+  const int sms = kf::sm_count_current_device();
+  const int G = Hq / Hkv;
+  int parts_max = 1, part_chunk = nqb;
+  const size_t split_need = 256 + acc_bytes + 2 * row_bytes + 2 * kv_acc_bytes;
+  if (causal && (int64_t)B * Hkv * nkb < 2 * (int64_t)sms && workspace_bytes >= split_need) {
+    int64_t total = 0;  // steps of the whole launch (query block x head per key block)
+    for (int n = 0; n < nkb; ++n) total += (int64_t)G * (nqb - std::min((n * kBN) / kBM, nqb));
+    total *= (int64_t)B * Hkv;
+    const int64_t target = (total + 2 * sms - 1) / (2 * sms);
+    part_chunk = (int)std::max<int64_t>(4, (target + G - 1) / G);
+    parts_max = (nqb + part_chunk - 1) / part_chunk;
+    if (parts_max <= 1) {
+      parts_max = 1;
+      part_chunk = nqb;
+    }
+  }
+  const bool split = parts_max > 1;
 
   PrepArgs pa;
   pa.o = static_cast<const uint16_t*>(o->ptr);
@@ -658,13 +775,22 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   pa.rows = (int64_t)B * Hq * Sq_pad;
   pa.acc = reinterpret_cast<float4*>(dq_acc);
   pa.acc_vec4 = (int64_t)B * Hq * nqb * D * kBM / 4;
+  pa.acc2 = split ? reinterpret_cast<float4*>(dk_acc) : nullptr;
+  pa.acc2_vec4 = split ? (int64_t)(2 * kv_acc_bytes) / 16 : 0;
   const int64_t prep_blocks = std::min<int64_t>((pa.rows + 15) / 16, (int64_t)kf::sm_count_current_device() * 8);
   prep_kernel<BF16><<<(unsigned)std::max<int64_t>(prep_blocks, 1), 256, 0, st>>>(pa);
   int rc = kf::check_launch("kf_attn_bwd prep");
   if (rc) return rc;
 
-  CUtensorMap mq, mk, mv, mdo, mdq;
+  CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   if ((rc = kf::encode_tmap_2d_f32(&mdq, dq_acc, (int64_t)B * Hq * nqb * D, kBM, 32, D))) return rc;
+  if (split) {
+    if ((rc = kf::encode_tmap_2d_f32(&mdk, dk_acc, (int64_t)B * Hkv * Sk_pad, D, 32, kBN))) return rc;
+    if ((rc = kf::encode_tmap_2d_f32(&mdv, dv_acc, (int64_t)B * Hkv * Sk_pad, D, 32, kBN))) return rc;
+  } else {
+    mdk = mdq;  // unused without a split
+    mdv = mdq;
+  }
   if ((rc = kf::encode_tmap_4d(&mq, q, 64, kBM))) return rc;
   if ((rc = kf::encode_tmap_4d(&mdo, dout, 64, kBM))) return rc;
   if ((rc = kf::encode_tmap_4d(&mk, k, 64, kBN))) return rc;
@@ -691,11 +817,34 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   p.nqb = nqb;
   p.nkb = nkb;
   p.pairs_per_group = kPairsPerGroup;
+  p.parts_max = parts_max;
+  p.part_chunk = part_chunk;
+  p.Sk_pad = Sk_pad;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * kLog2e;
   p.scale = scale;
   p.status = status;
-  if ((rc = dispatch_bwd_main<BF16>((D + 15) / 16, mq, mk, mv, mdo, mdq, p, st))) return rc;
+  if ((rc = dispatch_bwd_main<BF16>((D + 15) / 16, mq, mk, mv, mdo, mdq, mdk, mdv, p, st))) return rc;
+  if (split) {
+    FinishKVArgs fk;
+    fk.acc_k = dk_acc;
+    fk.acc_v = dv_acc;
+    fk.dk = static_cast<uint16_t*>(dk->ptr);
+    fk.dv = static_cast<uint16_t*>(dv->ptr);
+    for (int i = 0; i < 4; ++i) {
+      fk.dks[i] = dk->stride[i];
+      fk.dvs[i] = dv->stride[i];
+    }
+    fk.Hkv = Hkv;
+    fk.Sk = Sk;
+    fk.Sk_pad = Sk_pad;
+    fk.D = D;
+    fk.scale = scale;
+    fk.rows = (int64_t)B * Hkv * Sk;
+    const int64_t blocks = std::min<int64_t>((2 * fk.rows * (D / 8) + 255) / 256, (int64_t)sms * 8);
+    finish_kv_kernel<BF16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(fk);
+    if ((rc = kf::check_launch("kf_attn_bwd finish dK/dV"))) return rc;
+  }
 
   FinishArgs fa;
   fa.acc = dq_acc;
@@ -715,6 +864,12 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
 extern "C" size_t kf_attn_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t D) {
   const int64_t Sq_pad = (Sq + kBM - 1) / kBM * kBM;
   return 256 + align256((size_t)(B * Hq * Sq_pad) * D * 4) + 2 * align256((size_t)(B * Hq * Sq_pad) * 4);
+}
+
+extern "C" size_t kf_attn_bwd_workspace_bytes_kv(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk,
+                                                 int64_t D) {
+  const int64_t Sk_pad = (Sk + kBN - 1) / kBN * kBN;
+  return kf_attn_bwd_workspace_bytes(B, Hq, Sq, D) + 2 * align256((size_t)(B * Hkv * Sk_pad) * D * 4);
 }
 
 extern "C" int kf_attn_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v,
@@ -753,6 +908,6 @@ extern "C" int kf_attn_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   if (guard.status()) return guard.status();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == KF_BF16)
-    return run_bwd<true>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, status, st);
-  return run_bwd<false>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, status, st);
+    return run_bwd<true>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, workspace_bytes, status, st);
+  return run_bwd<false>(q, k, v, o, lse, dout, dq, dk, dv, scale, causal, workspace, workspace_bytes, status, st);
 }
