@@ -1053,6 +1053,18 @@ def run_decode_case(args, world, rank):
 
 
 # --------------------------------------------------------------------------- main
+def guarded(fn, *args, **kwargs):
+    """Run an optional sub-benchmark; an exception becomes {"error": ...} in
+    the line instead of ending the run (the headline is already measured).
+    Every rank runs the same code, so a failure in a collective sub-benchmark
+    is met by every rank alike."""
+    try:
+        return fn(*args, **kwargs)
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        print(f"{getattr(fn, '__name__', fn)} failed: {type(exc).__name__}: {exc}", file=sys.stderr, flush=True)
+        return {"error": f"{type(exc).__name__}: {str(exc).splitlines()[0][:200] if str(exc) else ''}"}
+
+
 def detail(name, payload):
     """A detail line (no "metric" key): printed before the headline line."""
     print(json.dumps({"detail": name, "data": payload}), flush=True)
@@ -1146,20 +1158,21 @@ def main(argv=None) -> int:
         "step_frac": round(value / world / peak, 4),
     }
 
-    fp16 = None if args.only_prefill else bench_fp16_prefill(args, world, peaks)
-    odd = [] if args.only_prefill else bench_odd_head_dim(peaks, world, rank)
-    parity = bench_parity() if (rank == 0 and not args.no_parity) else None
+    fp16 = None if args.only_prefill else guarded(bench_fp16_prefill, args, world, peaks)
+    odd = [] if args.only_prefill else guarded(bench_odd_head_dim, peaks, world, rank)
+    parity = guarded(bench_parity) if (rank == 0 and not args.no_parity) else None
 
     decode = None
     multi = None
     if not args.no_decode:
         if world > 1:
-            multi = bench_decode_multi_gpu(world, rank)
+            multi = guarded(bench_decode_multi_gpu, world, rank)
         elif rank == 0:
-            decode = {"sweep": bench_decode_sweep(peaks), "kv_cache_loop": bench_cache_loop(peaks)}
-    comparators = (bench_sdpa_comparators(dtype)
+            decode = {"sweep": guarded(bench_decode_sweep, peaks), "kv_cache_loop": guarded(bench_cache_loop, peaks)}
+    comparators = (guarded(bench_sdpa_comparators, dtype)
                    if (rank == 0 and world == 1 and not args.no_comparators) else None)
-    block = ({"fp32_projections": bench_decoder_block(), "bf16_block": bench_decoder_block(bf16_block=True)}
+    block = ({"fp32_projections": guarded(bench_decoder_block),
+              "bf16_block": guarded(bench_decoder_block, bf16_block=True)}
              if (rank == 0 and world == 1 and not args.no_comparators) else None)
 
     cpu = None
@@ -1173,27 +1186,35 @@ def main(argv=None) -> int:
     if rank == 0:
         if decode is not None:
             detail("decode_sweep", decode["sweep"])
-        if odd:
+        if odd and not isinstance(odd, dict):
             detail("odd_head_dim_training", odd)
         if comparators is not None:
             detail("gpu_comparators", comparators)
         if block is not None:
             detail("decoder_block_training_step", block)
-        if parity is not None and not parity["pass"]:
+        if parity is not None and not parity.get("pass", False):
             print("parity check FAILED: " + json.dumps(parity), file=sys.stderr, flush=True)
         dec = None
         if decode is not None:
-            keep = [r for r in decode["sweep"] if r["sq"] == 1 or r["sk"] >= 32768]
-            loop = decode["kv_cache_loop"]
-            dec = {"cols": "sq,sk,us_per_call,us_per_token,hbm_frac",
-                   "rows": [[r["sq"], r["sk"], r["us_per_call"], r["us_per_token"], r["hbm_frac"]] for r in keep],
-                   "kv_cache_loop": {"us_per_token": loop["us_per_token"], "hbm_frac": loop["hbm_frac"],
-                                     "prefill_append_hbm_frac": loop["prefill_append"]["hbm_frac"],
-                                     "append_bit_exact": loop["append_bit_exact"]}}
-        cfg5 = None if not odd else {
-            "cols": "d,causal,ms,fwd_bwd_tflops,per_rank_frac",
-            "rows": [[r["d"], int(r["causal"]), r["ms"], r["fwd_bwd_tflops"], r["per_rank_frac"]] for r in odd],
-            "units_per_rank": odd[0]["units_per_rank"], "scaling": "strong (8 units over the ranks)"}
+            dec = {}
+            sweep, loop = decode["sweep"], decode["kv_cache_loop"]
+            if isinstance(sweep, dict):
+                dec["sweep"] = sweep
+            else:
+                keep = [r for r in sweep if r["sq"] == 1 or r["sk"] >= 32768]
+                dec["cols"] = "sq,sk,us_per_call,us_per_token,hbm_frac"
+                dec["rows"] = [[r["sq"], r["sk"], r["us_per_call"], r["us_per_token"], r["hbm_frac"]] for r in keep]
+            dec["kv_cache_loop"] = loop if "error" in loop else {
+                "us_per_token": loop["us_per_token"], "hbm_frac": loop["hbm_frac"],
+                "prefill_append_hbm_frac": loop["prefill_append"]["hbm_frac"],
+                "append_bit_exact": loop["append_bit_exact"]}
+        if isinstance(odd, dict):
+            cfg5 = odd
+        else:
+            cfg5 = None if not odd else {
+                "cols": "d,causal,ms,fwd_bwd_tflops,per_rank_frac",
+                "rows": [[r["d"], int(r["causal"]), r["ms"], r["fwd_bwd_tflops"], r["per_rank_frac"]] for r in odd],
+                "units_per_rank": odd[0]["units_per_rank"], "scaling": "strong (8 units over the ranks)"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -1206,7 +1227,7 @@ def main(argv=None) -> int:
                        "l2": "inputs larger than L2 (q/dO 134 MB each)"},
             "frac_of_peak": round(value / world / peak, 4),
             "roofline": roofline, "clocks": clocks,
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": 4 * args.steps,  # per step: forward, backward prep, main, finish
             "e2e": e2e, "cpu_baseline": cpu,
             # extras: the end of the line is what a 1500-character tail keeps
             "decode_multi_gpu": multi, "cfg5": cfg5, "fp16": fp16,

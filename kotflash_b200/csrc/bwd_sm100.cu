@@ -425,7 +425,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     bool ok = true;
     for (int s = 0; ok && s < nsteps; ++s) {
       const int buf = s & 1;  // TMEM buffer and shared-memory staging buffer
-      if (!(ok = wait_bar(&bars->dq_full[buf], (s >> 1) & 1, bars, p.status))) break;
+      // one decision for the whole warpgroup (its named barriers below must
+      // see every thread), even if one thread's bounded wait gave up
+      ok = kf::named_bar_and(1, 128, wait_bar(&bars->dq_full[buf], (s >> 1) & 1, bars, p.status));
+      if (!ok) break;
       kf::tc_fence_after();
       uint32_t v[64];
       kf::tmem_ld32(lane_base + kColDP + buf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));

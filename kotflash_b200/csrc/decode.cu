@@ -782,22 +782,33 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
         const bool row_ok = r < valid_rows;
         const int pr = row0 + r;
         const int64_t prow = (int64_t)(b * a.Hkv + kvh) * a.rows + pr;
-        for (int c0 = 0; c0 < d_pad16; c0 += 16) {
-          uint32_t ov[16];
-          kf::tmem_ld16(lane_base + 128 + c0, ov);
+        // O in 64-column batches: up to four 16-column loads in flight per
+        // wait (one TMEM round trip per batch, on the tail of every split)
+#pragma unroll
+        for (int c0 = 0; c0 < d_pad16; c0 += 64) {
+          uint32_t ov[64];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            if (c0 + 16 * q4 < d_pad16) {
+              kf::tmem_ld16(lane_base + 128 + c0 + 16 * q4, *reinterpret_cast<uint32_t(*)[16]>(&ov[16 * q4]));
+            } else {
+#pragma unroll
+              for (int c = 0; c < 16; ++c) ov[16 * q4 + c] = 0u;
+            }
+          }
           kf::tmem_wait_ld();
           if (!row_ok) continue;
           if (a.direct) {
             uint16_t* dst = a.o + b * a.os[0] + (int64_t)(kvh * a.G + pr / a.Sq) * a.os[1] + (pr % a.Sq) * a.os[2];
 #pragma unroll
-            for (int c = 0; c < 16; c += 2)
+            for (int c = 0; c < 64; c += 2)
               if (c0 + c < a.D)
                 *reinterpret_cast<uint32_t*>(dst + c0 + c) =
                     kf::pack2<BF16>(__uint_as_float(ov[c]) * inv_l, __uint_as_float(ov[c + 1]) * inv_l);
           } else {
             float* dst = a.part_o + ((int64_t)split * a.prow_total + prow) * a.D;
 #pragma unroll
-            for (int c = 0; c < 16; c += 4)
+            for (int c = 0; c < 64; c += 4)
               if (c0 + c < a.D)
                 *reinterpret_cast<float4*>(dst + c0 + c) =
                     make_float4(__uint_as_float(ov[c]) * inv_l, __uint_as_float(ov[c + 1]) * inv_l,

@@ -501,17 +501,26 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
         const bool row_ok = row < p.Sq;
         uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)my_head * p.os[1] + (int64_t)row * p.os[2];
-        for (int c0 = 0; c0 < d_pad16; c0 += 32) {
-          uint32_t ov[32];
-          kf::tmem_ld32(lane_base + o_col + c0, ov);
-          kf::tmem_wait_ld();
-          uint32_t pk[16];
+        // O in 64-column halves: both 32-column loads of a half are in flight
+        // before one wait (one TMEM round trip per half, not per 32 columns)
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
+        for (int c0 = 0; c0 < d_pad16; c0 += 64) {
+          uint32_t ov[64];
+          kf::tmem_ld32(lane_base + o_col + c0, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+          if (c0 + 32 < d_pad16) {
+            kf::tmem_ld32(lane_base + o_col + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+          } else {
+#pragma unroll
+            for (int c = 32; c < 64; ++c) ov[c] = 0u;
+          }
+          kf::tmem_wait_ld();
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
             pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * inv_l, __uint_as_float(ov[2 * c + 1]) * inv_l);
           if (row_ok) {
 #pragma unroll
-            for (int g8 = 0; g8 < 4; ++g8) {
+            for (int g8 = 0; g8 < 8; ++g8) {
               if (c0 + g8 * 8 < p.D)
                 *reinterpret_cast<uint4*>(orow_g + c0 + g8 * 8) =
                     make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);

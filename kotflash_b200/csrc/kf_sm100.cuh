@@ -216,6 +216,20 @@ KF_DEVI void bulk_wait_group() {
 KF_DEVI void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// The same barrier returning the AND of every participant's `pred`, so that
+// threads whose own bounded waits disagree still leave with one decision.
+KF_DEVI bool named_bar_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 // ---------------------------------------------------------------- tcgen05
 // Tensor memory address: bits [31:16] lane, [15:0] column.
