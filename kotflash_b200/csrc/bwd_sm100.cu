@@ -489,15 +489,24 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       // with TMA reduce-add; the finish kernel converts the sums.
       uint8_t* stage = is_dk ? sK : sQ;
       if (have) {
-        for (int c0 = 0; c0 < d_pad16; c0 += 32) {
-          uint32_t ov[32];
-          kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0, ov);
-          kf::tmem_wait_ld();
-          uint8_t* row_ptr = stage + (c0 >> 5) * (kBN * 128) + kr * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(row_ptr + ((j ^ (kr & 7)) << 4)) =
-                make_uint4(ov[4 * j], ov[4 * j + 1], ov[4 * j + 2], ov[4 * j + 3]);
+        for (int c0 = 0; c0 < d_pad16; c0 += 64) {
+          uint32_t ov[64];
+          const bool two = c0 + 32 < d_pad16;
+          kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+          if (two)
+            kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+          kf::tmem_wait_ld();
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            if (hb == 1 && !two) break;
+            uint8_t* row_ptr = stage + ((c0 >> 5) + hb) * (kBN * 128) + kr * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(row_ptr + ((j ^ (kr & 7)) << 4)) =
+                  make_uint4(ov[32 * hb + 4 * j], ov[32 * hb + 4 * j + 1], ov[32 * hb + 4 * j + 2],
+                             ov[32 * hb + 4 * j + 3]);
+          }
         }
         kf::fence_proxy_async_smem();
       }
@@ -510,22 +519,25 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         kf::bulk_wait_group<0>();
       }
     } else if (nsteps == 0 || have) {
-      for (int c0 = 0; c0 < d_pad16; c0 += 32) {
-        uint32_t ov[32];
+      // 64-column batches: two TMEM loads in flight per wait
+#pragma unroll
+      for (int c0 = 0; c0 < d_pad16; c0 += 64) {
+        uint32_t ov[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) ov[c] = 0u;
         if (have) {
-          kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0, ov);
+          kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+          if (c0 + 32 < d_pad16)
+            kf::tmem_ld32(lane_base + (is_dk ? kColDK : kColDV) + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
           kf::tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) ov[c] = 0u;
         }
-        uint32_t pk[16];
+        uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
+        for (int c = 0; c < 32; ++c)
           pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * mul, __uint_as_float(ov[2 * c + 1]) * mul);
         if (key < p.Sk) {
 #pragma unroll
-          for (int g8 = 0; g8 < 4; ++g8)
+          for (int g8 = 0; g8 < 8; ++g8)
             if (c0 + g8 * 8 < p.D)
               *reinterpret_cast<uint4*>(dst + c0 + g8 * 8) =
                   make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);
