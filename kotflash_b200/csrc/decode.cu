@@ -127,6 +127,18 @@ decode_split_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_cons
     abort_any = 0;
     kf::tma_prefetch_desc(&map_k);
     kf::tma_prefetch_desc(&map_v);
+    // the first tiles' HBM latency overlaps the previous kernel's tail (an
+    // L2 prefetch only hints: L2 stays coherent with that kernel's writes)
+    for (int t = 0; t < STAGES && t < n_tiles; ++t)
+#pragma unroll
+      for (int pn = 0; pn < NP; ++pn) {
+        kf::tma_prefetch_l2_4d(&map_k, pn * 64, key_begin + t * TN, kvh, b);
+        kf::tma_prefetch_l2_4d(&map_v, pn * 64, key_begin + t * TN, kvh, b);
+      }
+  }
+  if (tid < ROWS && row0 + tid < a.rows) {
+    const int pr = row0 + tid, g = pr / a.Sq, s = pr % a.Sq;
+    kf::prefetch_l2_bulk(a.q + b * a.qs[0] + (int64_t)(kvh * a.G + g) * a.qs[1] + s * a.qs[2], a.D * 2);
   }
   // Launched with programmatic stream serialization: everything above ran
   // while the previous kernel of the stream may still be finishing; nothing
@@ -531,6 +543,10 @@ constexpr int kTcThreads = 192;
 constexpr int kTcKeys = 64;    // keys per K/V tile and per S buffer
 constexpr int kTcStages = 4;
 constexpr float kTcRescale = 8.0f;  // log2 units, as in the prefill forward
+#ifndef KF_DEC_POLY_PAIRS
+#define KF_DEC_POLY_PAIRS 2
+#endif
+constexpr int kTcPolyPairs = KF_DEC_POLY_PAIRS;  // of every 8 exponential pairs
 
 struct __align__(8) TcBarriers {
   uint64_t full[kTcStages], empty[kTcStages];
@@ -604,6 +620,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
   if (warp == 5 && lane == 0) {
     kf::tma_prefetch_desc(&map_k);
     kf::tma_prefetch_desc(&map_v);
+    // the first tiles' HBM latency overlaps the previous kernel's tail
+    for (int t = 0; t < kTcStages && t < n_tiles; ++t)
+      for (int pn = 0; pn < NP; ++pn) {
+        kf::tma_prefetch_l2_4d(&map_k, pn * 64, key_begin + t * kTcKeys, kvh, b);
+        kf::tma_prefetch_l2_4d(&map_v, pn * 64, key_begin + t * kTcKeys, kvh, b);
+      }
+  }
+  if (tid < valid_rows) {
+    const int pr = row0 + tid, g = pr / a.Sq, s = pr % a.Sq;
+    kf::prefetch_l2_bulk(a.q + b * a.qs[0] + (int64_t)(kvh * a.G + g) * a.qs[1] + s * a.qs[2], a.D * 2);
   }
   kf::tc_fence_before();
   __syncthreads();
@@ -743,13 +769,30 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
         const uint64_t scl = kf::f2(a.scale_log2, a.scale_log2), negm = kf::f2(-m_use, -m_use);
         uint32_t pk[kTcKeys / 2];
         uint64_t acc[2] = {0ull, 0ull};
+        if (lim < kTcKeys) {
+          // masked tile (-inf entries): MUFU only
 #pragma unroll
-        for (int c = 0; c < kTcKeys / 2; ++c) {
-          float x0, x1;
-          kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
-          const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
-          acc[c & 1] = kf::add2(acc[c & 1], kf::f2(p0, p1));
-          pk[c] = kf::pack2<BF16>(p0, p1);
+          for (int c = 0; c < kTcKeys / 2; ++c) {
+            float x0, x1;
+            kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+            const float p0 = kf::ex2(x0), p1 = kf::ex2(x1);
+            acc[c & 1] = kf::add2(acc[c & 1], kf::f2(p0, p1));
+            pk[c] = kf::pack2<BF16>(p0, p1);
+          }
+        } else {
+          // full tile: kTcPolyPairs of every 8 pairs on the fp32-pipe
+          // polynomial, the rest on MUFU (with one live softmax warp per SM
+          // sub-partition the exponentials are MUFU-bound otherwise)
+#pragma unroll
+          for (int c = 0; c < kTcKeys / 2; ++c) {
+            float x0, x1;
+            kf::f2_split(kf::fma2(kf::f2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), scl, negm), x0, x1);
+            const uint64_t pp = (c & 7) < kTcPolyPairs ? kf::exp2_poly2(x0, x1) : kf::f2(kf::ex2(x0), kf::ex2(x1));
+            acc[c & 1] = kf::add2(acc[c & 1], pp);
+            float p0, p1;
+            kf::f2_split(pp, p0, p1);
+            pk[c] = kf::pack2<BF16>(p0, p1);
+          }
         }
         {
           float s0, s1;

@@ -20,10 +20,9 @@
 //
 // Each tile has its own score buffer S, probability buffer P (16-bit) and
 // output accumulator O in tensor memory (512 columns):
-//   BN = 80 keys per block (head_dim > 64):
-//     S0 [0,80) P0 [80,120) S1 [128,208) P1 [208,248) O0 [256,384) O1 [384,512)
-//   BN = 128 keys per block (head_dim <= 64):
-//     S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384) P0 [384,448) P1 [448,512)
+//   head_dim <= 64  (BN 128): S0 [0,128)  P0 [128,192)  O0 [192,256)  S1 [256,384)  P1 [384,448)  O1 [448,512)
+//   head_dim 65-96  (BN  96): S0 [0,96)   P0 [96,144)   O0 [160,256)  S1 [256,352)  P1 [352,400)  O1 [416,512)
+//   head_dim 97-128 (BN  80): S0 [0,80)   P0 [80,120)   O0 [128,256)  S1 [256,336)  P1 [336,376)  O1 [384,512)
 // Because P does not overlay S, a tile's softmax releases S as soon as it has
 // loaded the scores into registers, and the tile's issuer computes the next
 // block's S = Q K^T while the softmax still works on this block; P feeds the
@@ -33,9 +32,11 @@
 // so the softmax of a tile runs block after block without waiting for its own
 // GEMMs, and the two tiles' GEMMs fill the tensor pipe between them.  With
 // P over S (an earlier layout) each tile's chain was softmax + its two GEMMs
-// in series, and the tensor pipe sat idle about half the time.  80 keys is the
-// widest block whose S and P fit beside a 128-column O (2 x (80 + 40 + 128)
-// <= 512); Q K^T with N = 80 costs a little shared-memory bandwidth per FLOP.
+// in series, and the tensor pipe sat idle about half the time.  The block
+// width is the widest multiple of 16 for which a tile's S and P fit below its
+// O in 256 columns (80 + 40 + 128 at head_dim 128, 96 + 48 + 96 at head_dim
+// 96); fewer keys per block cost a little shared-memory bandwidth per FLOP
+// and more per-block synchronisation.
 // Two issuing threads matter on sm_100: the tensor pipe holds almost no
 // queued MMAs, so every cycle an issuing thread spends on an mbarrier wait, a
 // tcgen05 fence or a commit would idle the pipe; with one issuer per tile,
@@ -88,15 +89,37 @@ struct FwdParams {
   int32_t* status;
 };
 
-// Keys per K/V block and K/V ring depth for a head dim of KS * 16: 80-key
-// blocks when O needs 128 TMEM columns, 128 otherwise (layouts above).
-__host__ __device__ constexpr int block_n(int ks) { return ks > 4 ? 80 : 128; }
+// Keys per K/V block, K/V ring depth and TMEM columns of each tile's S, P and
+// O for a head dim of KS * 16 (layouts above).  Tile t owns columns
+// [256 t, 256 t + 256): S at the bottom, P right above it, O at the top
+// (its width rounded up to 32 columns).  The block width is the widest
+// multiple of 16 whose S and P fit below O.  (A layout with S and P of both
+// tiles in the low 256 columns and both O in the high 256 measured the same
+// at head_dim 128 and 2-5% slower at 72 and 96, interleaved in one process.)
+__host__ __device__ constexpr int block_n(int ks) { return ks > 6 ? 80 : (ks > 4 ? 96 : 128); }
 __host__ __device__ constexpr int kv_stages(int ks) { return ks > 4 ? 3 : 4; }
-__host__ __device__ constexpr uint32_t s_col_of(int bn, int t) { return (uint32_t)(t * 128 + 0 * bn); }
-__host__ __device__ constexpr uint32_t p_col_of(int bn, int t) {
-  return bn == 128 ? 384u + 64u * t : (uint32_t)(t * 128 + bn);
+__host__ __device__ constexpr int o_width(int ks) { return (ks * 16 + 31) / 32 * 32; }
+__host__ __device__ constexpr uint32_t s_col_of(int ks, int t) { return 256u * t + 0u * ks; }
+__host__ __device__ constexpr uint32_t p_col_of(int ks, int t) { return 256u * t + block_n(ks); }
+__host__ __device__ constexpr uint32_t o_col_of(int ks, int t) { return 256u * t + 256u - o_width(ks); }
+// The six buffers of a layout are disjoint and inside the 512 columns.
+__host__ __device__ constexpr bool disjoint(uint32_t a, uint32_t an, uint32_t b, uint32_t bn) {
+  return a + an <= b || b + bn <= a;
 }
-__host__ __device__ constexpr uint32_t o_col_of(int bn, int t) { return bn == 128 ? 256u + 64u * t : 256u + 128u * t; }
+__host__ __device__ constexpr bool layout_ok(int ks) {
+  const uint32_t bn = block_n(ks), w[3] = {bn, bn / 2, (uint32_t)o_width(ks)};
+  uint32_t c[6] = {s_col_of(ks, 0), p_col_of(ks, 0), o_col_of(ks, 0),
+                   s_col_of(ks, 1), p_col_of(ks, 1), o_col_of(ks, 1)};
+  for (int i = 0; i < 6; ++i) {
+    if (c[i] + w[i % 3] > 512u) return false;
+    for (int j = i + 1; j < 6; ++j)
+      if (!disjoint(c[i], w[i % 3], c[j], w[j % 3])) return false;
+  }
+  return true;
+}
+static_assert(layout_ok(1) && layout_ok(2) && layout_ok(3) && layout_ok(4) && layout_ok(5) &&
+                  layout_ok(6) && layout_ok(7) && layout_ok(8),
+              "TMEM layout");
 
 struct __align__(8) FwdBarriers {
   uint64_t q_full, q_empty;
@@ -286,7 +309,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const kf::SDesc dq = kf::make_sdesc_split(kf::smem_u32(sQ + t * QTILE), 16, 1024);
       const kf::SDesc dk = kf::make_sdesc_split(kf::smem_u32(sK), 16, 1024);
       const kf::SDesc dv = kf::make_sdesc_split(kf::smem_u32(sV), KPANEL, 1024);
-      const uint32_t s_tm = tmem + s_col_of(BN, t), p_tm = tmem + p_col_of(BN, t), o_tm = tmem + o_col_of(BN, t);
+      const uint32_t s_tm = tmem + s_col_of(KS, t), p_tm = tmem + p_col_of(KS, t), o_tm = tmem + o_col_of(KS, t);
       // Each GEMM is one straight-line run of MMAs (compile-time trip counts).
       auto issue_qk = [&](int gj) {
         const uint32_t koff = (gj % STAGES) * KTILE;
@@ -361,7 +384,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     const int t = warp >> 2;        // tile handled by this warpgroup
     const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t s_col = s_col_of(BN, t), p_col = p_col_of(BN, t), o_col = o_col_of(BN, t);
+    const uint32_t s_col = s_col_of(KS, t), p_col = p_col_of(KS, t), o_col = o_col_of(KS, t);
     int jt = 0, vt = 0, jturn = 0;  // blocks of tile t, items of tile t, blocks of two-tile items
     bool ok = true;
     for (int rd = 0; ok && rd < rounds; ++rd) {
@@ -387,7 +410,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         if constexpr (BN == 128) {
           kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
           kf::tmem_ld32(lane_base + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        } else if constexpr (BN == 96) {
+          kf::tmem_ld32(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
         } else {
+          static_assert(BN == 80, "block width");
           kf::tmem_ld16(lane_base + s_col + 64, *reinterpret_cast<uint32_t(*)[16]>(&sr[64]));
         }
         kf::tmem_wait_ld();
@@ -475,6 +501,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         kf::tmem_st32(lane_base + p_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
         if constexpr (BN == 128) {
           kf::tmem_st32(lane_base + p_col + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        } else if constexpr (BN == 96) {
+          kf::tmem_st16(lane_base + p_col + 32, *reinterpret_cast<const uint32_t(*)[16]>(&pk[32]));
         } else {
           kf::tmem_st8(lane_base + p_col + 32, *reinterpret_cast<const uint32_t(*)[8]>(&pk[32]));
         }

@@ -194,6 +194,23 @@ KF_DEVI void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, 
       : "memory");
 }
 
+// Prefetch one 4-D tile of a tensor map into L2.  It returns nothing and
+// completes nothing, so it is only a hint: L2 stays coherent with every later
+// write, and the hint may be issued before griddep_wait().
+KF_DEVI void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+// Prefetch `bytes` (a multiple of 16, 16-byte aligned) of global memory into
+// L2; a hint like tma_prefetch_l2_4d.
+KF_DEVI void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
+}
+
 // 2-D tiled reduce-add of an fp32 tile, this CTA's shared memory -> global,
 // tracked by the bulk-async group of the issuing thread.
 KF_DEVI void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
