@@ -1100,6 +1100,9 @@ def main(argv=None) -> int:
     ap.add_argument("--only-prefill", action="store_true",
                     help="time only the headline prefill step (no fp16, cfg5, parity, decode, e2e, CPU or "
                          "comparator legs): the short command the ncu captures in profiles/ use")
+    ap.add_argument("--only-odd-head-dim", action="store_true",
+                    help="time only the odd-head-dim training config (BASELINE configs[4], sharded over "
+                         "the ranks) and print its detail line: the command the cfg5 ncu captures use")
     ap.add_argument("--decode-case", default=None, metavar="SQ,SK",
                     help="time only the split-KV decode config (B2 Hq8 Hkv2 D64 fp16) at one "
                          "(Sq, Sk) with --warmup/--steps plain launches; prints one JSON line")
@@ -1120,6 +1123,16 @@ def main(argv=None) -> int:
     _ext.load()  # fail loudly when the kernel library is missing
     if args.decode_case:
         return run_decode_case(args, world, rank)
+    if args.only_odd_head_dim:
+        res = bench_odd_head_dim(load_peaks(), world, rank)
+        if rank == 0:
+            detail("odd_head_dim_training", res)
+        if world > 1:
+            import torch.distributed as dist
+
+            barrier(world)
+            dist.destroy_process_group()
+        return 0
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     peaks = load_peaks()
     ms_step, fwd_ms, bwd_ms, clocks = bench_prefill(args, world, rank, local, dtype)
