@@ -229,14 +229,19 @@ template <int N>
 KF_DEVI void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
-// Named barrier among `nthreads` threads (a multiple of 32).
+// Named barrier among `nthreads` threads (a multiple of 32), called by whole
+// warps.  bar.sync / bar.red are the .aligned barrier forms: every thread of
+// a warp must reach them converged, so the warp is reconverged first (the
+// callers arrive from per-lane spin loops, which may leave it diverged).
 KF_DEVI void named_bar_sync(int id, int nthreads) {
+  __syncwarp();
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 // The same barrier returning the AND of every participant's `pred`, so that
 // threads whose own bounded waits disagree still leave with one decision.
 KF_DEVI bool named_bar_and(int id, int nthreads, bool pred) {
   uint32_t r;
+  __syncwarp();
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
