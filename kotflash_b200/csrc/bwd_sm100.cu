@@ -345,7 +345,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       for (int c4 = 0; c4 < 8; ++c4) lv[c4] = lse4[c4];
       const int q0 = i_step * kBM + c0;
       const uint32_t col_s = kColS + buf * 64;
-      if (!(ok = wait_bar(&bars->s_ready[buf], (s >> 1) & 1, bars, p.status))) break;
+      if (!(ok = __all_sync(0xffffffffu, wait_bar(&bars->s_ready[buf], (s >> 1) & 1, bars, p.status)))) break;
       kf::tc_fence_after();
       uint32_t sr[32];
       kf::tmem_ld32(lane_base + col_s + c0, sr);
@@ -390,7 +390,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const uint32_t col_dp = kColDP + buf * 64;
 #pragma unroll
       for (int c4 = 0; c4 < 8; ++c4) lv[c4] = dlt4[c4];
-      if (!(ok = wait_bar(&bars->dp_ready[buf], (s >> 1) & 1, bars, p.status))) break;
+      if (!(ok = __all_sync(0xffffffffu, wait_bar(&bars->dp_ready[buf], (s >> 1) & 1, bars, p.status)))) break;
       kf::tc_fence_after();
       uint32_t dr[32];
       kf::tmem_ld32(lane_base + col_dp + c0, dr);
@@ -479,7 +479,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     uint16_t* dst = is_dk ? p.dk + b * p.dks[0] + (int64_t)kvh * p.dks[1] + (int64_t)key * p.dks[2]
                           : p.dv + b * p.dvs[0] + (int64_t)kvh * p.dvs[1] + (int64_t)key * p.dvs[2];
     const float mul = is_dk ? p.scale : 1.f;
-    const bool have = nsteps > 0 && wait_bar(&bars->mma_done, 0, bars, p.status);
+    const bool have = __all_sync(0xffffffffu, nsteps > 0 && wait_bar(&bars->mma_done, 0, bars, p.status));
     if (have) kf::tc_fence_after();
     if (split) {
       // This CTA's part of dK/dV goes to the fp32 accumulators: each

@@ -732,7 +732,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
     bool ok = true;
     if (warp < active_warps) {
       for (int t = 0; ok && t < n_tiles; ++t) {
-        if (!(ok = tc_wait(&bars->s_full[t & 1], (t >> 1) & 1, bars, a.status))) break;
+        if (!(ok = __all_sync(0xffffffffu, tc_wait(&bars->s_full[t & 1], (t >> 1) & 1, bars, a.status)))) break;
         kf::tc_fence_after();
         const uint32_t s_col = (t & 1) * kTcKeys;
         uint32_t sr[kTcKeys];
@@ -802,7 +802,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
         kf::tmem_st32(lane_base + s_col, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
         if (__any_sync(0xffffffffu, rescale_o)) {
           // O row *= alpha once PV_{t-1} has landed (S_t was issued before it)
-          if (!(ok = tc_wait(&bars->pv_done, (t - 1) & 1, bars, a.status))) break;
+          if (!(ok = __all_sync(0xffffffffu, tc_wait(&bars->pv_done, (t - 1) & 1, bars, a.status)))) break;
           kf::tc_fence_after();
           for (int c0 = 0; c0 < d_pad16; c0 += 16) {
             uint32_t orow[16];
@@ -818,7 +818,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constan
         kf::mbar_arrive(&bars->p_full[t & 1]);
       }
       // ---------------------------------------------------------- epilogue
-      if (ok && tc_wait(&bars->o_done, 0, bars, a.status)) {
+      if (__all_sync(0xffffffffu, ok && tc_wait(&bars->o_done, 0, bars, a.status))) {
         kf::tc_fence_after();
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
         const float row_lse = l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;

@@ -402,7 +402,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       const int row = my_row0 + r;
       float m_ref = -INFINITY, l_sum = 0.f;
       for (int j = 0; ok && j < nblk; ++j) {
-        if (!(ok = wait_bar(&bars->s_full[t], (jt + j) & 1, bars, p.status))) break;
+        if (!(ok = __all_sync(0xffffffffu, wait_bar(&bars->s_full[t], (jt + j) & 1, bars, p.status)))) break;
         kf::tc_fence_after();
         uint32_t sr[BN];
         kf::tmem_ld32(lane_base + s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
@@ -495,7 +495,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
         // P(j) goes where P(j-1) was and O may be rescaled: both need the
         // previous block's O += P V to have completed
         if (j > 0) {
-          if (!(ok = wait_bar(&bars->pv_done[t], (jt + j - 1) & 1, bars, p.status))) break;
+          if (!(ok = __all_sync(0xffffffffu, wait_bar(&bars->pv_done[t], (jt + j - 1) & 1, bars, p.status)))) break;
           kf::tc_fence_after();
         }
         kf::tmem_st32(lane_base + p_col + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
@@ -524,7 +524,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       // -------------------------------------------------------- epilogue
       // O is read from TMEM before this thread's next p_full arrival, which
       // is what lets the next item's first PV overwrite it.
-      if (ok && (ok = wait_bar(&bars->o_final[t], vt & 1, bars, p.status))) {
+      if (ok && (ok = __all_sync(0xffffffffu, wait_bar(&bars->o_final[t], vt & 1, bars, p.status)))) {
         kf::tc_fence_after();
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
         const bool row_ok = row < p.Sq;
