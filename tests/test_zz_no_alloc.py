@@ -6,12 +6,14 @@ embedder with a fixed device-memory budget) give this library no allocator and
 no workspace.  kf_decode_noalloc keeps its split partials in a static 8 MiB
 device array instead.  This test calls it through the C ABI twice in a row,
 on different shapes, and checks each result against the workspace-taking
-kf_decode on the same inputs.  The file is named to be collected last.
+kf_decode on the same inputs and against the fp32 oracle.  The file is named
+to be collected last.
 """
 import pytest
 import torch
 
 from kotflash_b200 import _ext
+from oracle import attention_oracle as oracle
 from tests._util import TOL, check_close
 
 pytestmark = pytest.mark.gpu
@@ -64,6 +66,10 @@ def test_decode_noalloc_matches_decode_on_two_calls_in_a_row():
         torch.cuda.synchronize()
         check_close(got_o, want_o, name=f"no-alloc O {b},{hq},{hkv},{sq},{sk},{d}", atol=TOL, rtol=TOL)
         check_close(got_lse, want_lse, name=f"no-alloc LSE {b},{hq},{hkv},{sq},{sk},{d}", atol=TOL, rtol=TOL)
+        # and against the fp32 oracle directly, not only through kf_decode
+        exp_o, exp_lse = oracle.forward(q, k, v, causal=False, scale=d ** -0.5)
+        check_close(got_o, exp_o, name=f"no-alloc O vs oracle {b},{hq},{hkv},{sq},{sk},{d}")
+        check_close(got_lse, exp_lse, name=f"no-alloc LSE vs oracle {b},{hq},{hkv},{sq},{sk},{d}")
 
 
 def test_decode_noalloc_rejects_splits_beyond_the_static_scratch():
