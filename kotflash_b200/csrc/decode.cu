@@ -12,9 +12,11 @@
 //    that share a KV head are packed into one tile, so each K/V byte of the
 //    split is read from HBM exactly once (the reference reads it once per
 //    query head);
-//  * each of the 4 warps streams its own 16-key tiles (every 4th tile of the
-//    split) through a private cp.async ring of 16-byte loads into XOR-swizzled
-//    shared memory, so warps never wait on one another inside the loop;
+//  * one thread streams the split's K/V tiles by TMA (no multicast) into a
+//    shared ring of 64- or 128-key stages; each of the 4 warps takes its own
+//    quarter of the keys of every stage, and a stage is refilled once all
+//    four have left it; the first stages and the Q rows are prefetched into
+//    L2 before the dependent-launch wait;
 //  * QK^T and PV use warp-level m16n8k16 MMAs (ldmatrix operands) with an
 //    online softmax in the exp2 domain; the 4 warps' (m, l, O) are merged in
 //    shared memory at the end;
