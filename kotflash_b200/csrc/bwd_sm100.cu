@@ -748,18 +748,37 @@ int run_bwd(const kf_tensor4* q, const kf_tensor4* k, const kf_tensor4* v, const
   float* dk_acc = reinterpret_cast<float*>(ws + acc_bytes + 2 * row_bytes);
   float* dv_acc = reinterpret_cast<float*>(ws + acc_bytes + 2 * row_bytes + kv_acc_bytes);
 
-  // Query split of the key blocks, for causal problems with fewer key-block
-  // CTAs than two per SM (a long sequence sharded to one (batch, KV head)
-  // unit per GPU: key block 0 sees every query block, the last one almost
-  // none, so one CTA per key block would leave the grid waiting on its
-  // heaviest CTA).  Parts target about two waves of equal CTAs; they need
-  // the dK/dV accumulators, i.e. a workspace of
-  // kf_attn_bwd_workspace_bytes_kv bytes.
+  // Query split of the key blocks; the parts need the dK/dV accumulators,
+  // i.e. a workspace of kf_attn_bwd_workspace_bytes_kv bytes.
+  //  * Causal problems with fewer key-block CTAs than two per SM (a long
+  //    sequence sharded to one (batch, KV head) unit per GPU: key block 0
+  //    sees every query block, the last one almost none, so one CTA per key
+  //    block would leave the grid waiting on its heaviest CTA): parts target
+  //    about two waves of equal CTAs.
+  //  * Non-causal problems with few key blocks: every key-block CTA has the
+  //    same work, so what is lost is the last, partial wave of one CTA per
+  //    SM (128 key blocks on 148 SMs keep 87% of them busy); the key blocks
+  //    are cut into the number of parts (<= 16) that fills the waves best.
   const int sms = kf::sm_count_current_device();
   const int G = Hq / Hkv;
   int parts_max = 1, part_chunk = nqb;
   const size_t split_need = 256 + acc_bytes + 2 * row_bytes + 2 * kv_acc_bytes;
-  if (causal && (int64_t)B * Hkv * nkb < 2 * (int64_t)sms && workspace_bytes >= split_need) {
+  const int64_t kb_ctas = (int64_t)B * Hkv * nkb;
+  if (!causal && kb_ctas < 4 * (int64_t)sms && workspace_bytes >= split_need) {
+    auto fill = [&](int64_t ctas) { return (double)ctas / (double)(((ctas + sms - 1) / sms) * sms); };
+    double best_fill = fill(kb_ctas);
+    for (int want = 2; want <= 16 && nqb / want >= 4; ++want) {
+      const int chunk = (nqb + want - 1) / want;
+      const int parts = (nqb + chunk - 1) / chunk;  // parts of `chunk` query blocks
+      const double f = fill(kb_ctas * parts);
+      if (f > best_fill + 0.02) {
+        part_chunk = chunk;
+        parts_max = parts;
+        best_fill = f;
+      }
+    }
+  }
+  if (causal && kb_ctas < 2 * (int64_t)sms && workspace_bytes >= split_need) {
     int64_t total = 0;  // steps of the whole launch (query block x head per key block)
     for (int n = 0; n < nkb; ++n) total += (int64_t)G * (nqb - std::min((n * kBN) / kBM, nqb));
     total *= (int64_t)B * Hkv;

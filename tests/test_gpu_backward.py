@@ -116,13 +116,15 @@ def test_backward_odd_head_dim_full_length_unit(d, causal):
     check_close(dv, edv, name=f"{tag} dV")
 
 
+@pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("b,hq,hkv,s,d", [(1, 4, 1, 4096, 128), (2, 8, 2, 1000, 64), (1, 4, 2, 777, 96)])
-def test_backward_query_split_matches_single_cta_per_key_block(b, hq, hkv, s, d):
-    """A causal backward with fewer key-block CTAs than two per SM splits each
-    key block's query range over several CTAs when the workspace holds the
-    dK/dV accumulators (kf_attn_bwd_workspace_bytes_kv), and runs one CTA per
-    key block with the smaller kf_attn_bwd_workspace_bytes: both must match
-    the oracle (the split path of the reference is
+def test_backward_query_split_matches_single_cta_per_key_block(b, hq, hkv, s, d, causal):
+    """A backward with few key-block CTAs splits each key block's query range
+    over several CTAs when the workspace holds the dK/dV accumulators
+    (kf_attn_bwd_workspace_bytes_kv) -- causal grids to balance their unequal
+    key blocks, non-causal ones to fill the last wave of SMs -- and runs one
+    CTA per key block with the smaller kf_attn_bwd_workspace_bytes: both must
+    match the oracle (the split path of the reference is
     kotflash/kernels/triton_backward.py:199-332)."""
     from kotflash_b200 import _ext
 
@@ -132,7 +134,7 @@ def test_backward_query_split_matches_single_cta_per_key_block(b, hq, hkv, s, d)
     v = _rand((b, hkv, s, d), torch.bfloat16, 63)
     do = _rand((b, hq, s, d), torch.bfloat16, 64)
     scale = d ** -0.5
-    out, lse = attention_forward(q, k, v, causal=True, scale=scale)
+    out, lse = attention_forward(q, k, v, causal=causal, scale=scale)
     results = {}
     for name, ws_bytes in (("split", lib.kf_attn_bwd_workspace_bytes_kv(b, hq, hkv, s, s, d)),
                            ("single", lib.kf_attn_bwd_workspace_bytes(b, hq, s, d))):
@@ -141,13 +143,13 @@ def test_backward_query_split_matches_single_cta_per_key_block(b, hq, hkv, s, d)
         rc = lib.kf_attn_bwd(_ext.ref(_ext.t4(q)), _ext.ref(_ext.t4(k)), _ext.ref(_ext.t4(v)),
                              _ext.ref(_ext.t4(out)), lse.data_ptr(), _ext.ref(_ext.t4(do)),
                              _ext.ref(_ext.t4(dq)), _ext.ref(_ext.t4(dk)), _ext.ref(_ext.t4(dv)),
-                             _ext.KF_BF16, scale, 1, ws.data_ptr(), ws.numel(),
+                             _ext.KF_BF16, scale, int(causal), ws.data_ptr(), ws.numel(),
                              _ext.status_word(q.device).data_ptr(), _ext.stream_of(q))
         _ext.check(rc, "kf_attn_bwd")
         results[name] = (dq, dk, dv)
-    _, _, edq, edk, edv = oracle.forward_backward_chunked(q, k, v, do, causal=True, scale=scale)
+    _, _, edq, edk, edv = oracle.forward_backward_chunked(q, k, v, do, causal=causal, scale=scale)
     for name, (dq, dk, dv) in results.items():
-        tag = f"{name} {b},{hq},{hkv},{s},{d}"
+        tag = f"{name} {b},{hq},{hkv},{s},{d},causal={causal}"
         check_close(dq, edq, name=f"dQ {tag}")
         check_close(dk, edk, name=f"dK {tag}")
         check_close(dv, edv, name=f"dV {tag}")
