@@ -13,7 +13,8 @@ Sq=Sk=4096, D=128, bf16, q scaled by 1/sqrt(D), through the public
 FLOPs count only visible (q, k) pairs: fwd 4*B*Hq*D*P, bwd 2.5x fwd.
 
 Output: detail lines first (``{"detail": ...}``: the decode sweep, the
-odd-head-dim runs, the GPU comparators, the decoder-block step), then the
+odd-head-dim runs, the GPU comparators, the decoder-block step, the LM
+training A/B on a synthetic token stream), then the
 headline JSON line LAST, which also carries compact summaries:
   * ``parity``: max |err| of O, LSE, dQ, dK, dV against a chunked fp32
     reference computed on the GPU (cfg2 bf16 and fp16 batch 0, cfg5 one unit
@@ -50,6 +51,7 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -838,6 +840,169 @@ def bench_decoder_block(batch=2, seq=4096, q_heads=32, kv_heads=8, head_dim=128,
     return out
 
 
+# --------------------------------------------------------------------------- LM training A/B
+GPT2_VOCAB = 50257  # vocabulary size of the tokenizer the reference's LM benchmark uses ("gpt2")
+
+
+def synthetic_story_tokens(n, vocab=GPT2_VOCAB, seed=0):
+    """Seeded stand-in for a tokenized story corpus (the reference's LM A/B
+    streams TinyStories, which is not available offline): ``n`` token ids in
+    ``[0, vocab)`` with a Zipf-like unigram law (p(r) ~ (r + 10)^-1.1 over a
+    seeded ranking of the ids), a learnable bigram structure (with
+    probability 0.6 a token is followed by its fixed successor under a seeded
+    permutation) and an end-of-story id (``vocab - 1``) closing stories of
+    geometric length (mean 200 tokens).  Only the statistics are modelled;
+    no text of any corpus is involved."""
+    rng = np.random.default_rng(seed)
+    body = vocab - 1
+    p = 1.0 / (np.arange(body) + 10.0) ** 1.1
+    p /= p.sum()
+    ids_by_rank = rng.permutation(body)
+    draws = ids_by_rank[rng.choice(body, size=n, p=p)]
+    successor = rng.permutation(body)
+    follow = rng.random(n) < 0.6
+    story_end = rng.random(n) < 1.0 / 200.0
+    out = np.empty(n, dtype=np.int64)
+    prev = -1
+    for i in range(n):
+        if story_end[i]:
+            tok = body
+        elif prev >= 0 and prev != body and follow[i]:
+            tok = successor[prev]
+        else:
+            tok = draws[i]
+        out[i] = tok
+        prev = tok
+    return torch.from_numpy(out)
+
+
+class StoryLM(torch.nn.Module):
+    """Next-token LM of the reference's LM training A/B
+    (benchmarks/benchmark_tinystories_training.py:90-125): token and learned
+    position embeddings, ``layers`` pre-norm GQA decoder blocks with a SiLU-gated
+    MLP (the ``DecoderBlock`` above), a final LayerNorm and an output head tied
+    to the token embedding; N(0, 0.02) initialisation."""
+
+    def __init__(self, vocab, max_seq, layers=2, q_heads=8, kv_heads=2, head_dim=64, mlp_ratio=4):
+        super().__init__()
+        nn = torch.nn
+        hidden = q_heads * head_dim
+        self.tok = nn.Embedding(vocab, hidden)
+        self.pos = nn.Embedding(max_seq, hidden)
+        self.blocks = nn.ModuleList(DecoderBlock(q_heads, kv_heads, head_dim, mlp_ratio) for _ in range(layers))
+        self.norm = nn.LayerNorm(hidden)
+        for m in self.modules():
+            if isinstance(m, (nn.Linear, nn.Embedding)):
+                nn.init.normal_(m.weight, mean=0.0, std=0.02)
+
+    def forward(self, ids, backend):
+        import torch.nn.functional as F
+
+        x = self.tok(ids) + self.pos(torch.arange(ids.shape[1], device=ids.device))[None]
+        for blk in self.blocks:
+            x = blk(x, backend)
+        return F.linear(self.norm(x), self.tok.weight)
+
+
+def bench_story_lm_ab(seq=4096, batch=1, steps=100, warmup=5, lr=3e-4, weight_decay=0.01, seed=1337):
+    """LM training A/B of the reference's TinyStories benchmark on a synthetic
+    token stream of the same vocabulary: identical initial weights and
+    paired batches for both attention routes, fp32 master weights with fp16
+    autocast and a gradient scaler, AdamW, backend order shuffled per step;
+    CUDA-event step times (forward, cross-entropy, backward, optimizer) and
+    the evaluation loss on a held-out window before and after training.
+    Routes: this library (``backend="triton"``) and PyTorch SDPA on K/V
+    expanded to the query heads (the reference benchmark's baseline)."""
+    import random
+
+    import torch.nn.functional as F
+
+    n_train = (warmup + steps) * batch * seq + 1
+    stream = synthetic_story_tokens(n_train + batch * seq + 1, seed=seed)
+    train, held = stream[:n_train], stream[n_train:]
+    windows = train.unfold(0, batch * seq + 1, batch * seq)
+    order = torch.randperm(windows.shape[0], generator=torch.Generator().manual_seed(seed))
+    windows = windows[order].cuda()
+    xs = windows[:, :-1].reshape(-1, batch, seq)
+    ys = windows[:, 1:].reshape(-1, batch, seq)
+    ex = held[:-1].reshape(batch, seq).cuda()
+    ey = held[1:].reshape(batch, seq).cuda()
+
+    torch.manual_seed(seed)
+    init = StoryLM(GPT2_VOCAB, seq).state_dict()
+    routes = {"kotflash_b200": "kotflash_b200", "sdpa_expanded": "sdpa_expanded_kv"}
+    models, opts, scalers = {}, {}, {}
+    for name in routes:
+        m = StoryLM(GPT2_VOCAB, seq).cuda()
+        m.load_state_dict(init)
+        models[name] = m
+        opts[name] = torch.optim.AdamW(m.parameters(), lr=lr, weight_decay=weight_decay)
+        scalers[name] = torch.amp.GradScaler("cuda")
+
+    def loss_of(name, x, y):
+        with torch.autocast("cuda", dtype=torch.float16):
+            logits = models[name](x, routes[name])
+            return F.cross_entropy(logits.reshape(-1, logits.shape[-1]), y.reshape(-1))
+
+    def evaluate(name):
+        models[name].eval()
+        with torch.no_grad():
+            v = float(loss_of(name, ex, ey).float())
+        models[name].train()
+        return v
+
+    def step(name, x, y):
+        opts[name].zero_grad(set_to_none=True)
+        loss = loss_of(name, x, y)
+        scalers[name].scale(loss).backward()
+        scalers[name].step(opts[name])
+        scalers[name].update()
+        return loss.detach()
+
+    initial = {name: evaluate(name) for name in routes}
+    rng = random.Random(seed + 1)
+    for i in range(warmup):
+        names = list(routes)
+        rng.shuffle(names)
+        for name in names:
+            step(name, xs[i], ys[i])
+    torch.cuda.synchronize()
+    events = {name: [] for name in routes}
+    last = {}
+    for i in range(warmup, warmup + steps):
+        names = list(routes)
+        rng.shuffle(names)
+        for name in names:
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            last[name] = step(name, xs[i], ys[i])
+            e.record()
+            events[name].append((a, e))
+    torch.cuda.synchronize()
+    out = {"shape": {"batch": batch, "seq": seq, "layers": 2, "q_heads": 8, "kv_heads": 2, "head_dim": 64,
+                     "hidden": 512, "vocab": GPT2_VOCAB,
+                     "parameters": sum(p.numel() for p in models["kotflash_b200"].parameters())},
+           "data": "synthetic token stream (Zipf unigrams, seeded bigram successors, end-of-story id): "
+                   "stand-in for TinyStories, which needs a download",
+           "precision": "fp32 master weights, fp16 autocast, GradScaler; fp16 attention; AdamW",
+           "steps": steps, "warmup": warmup}
+    for name in routes:
+        times = [a.elapsed_time(e) for a, e in events[name]]
+        finite = bool(torch.isfinite(last[name]).all()) and all(
+            bool(torch.isfinite(p).all()) for p in models[name].parameters())
+        out[name] = {"median_step_ms": round(statistics.median(times), 3),
+                     "tokens_per_s": round(steps * batch * seq * 1e3 / sum(times), 1),
+                     "initial_eval_loss": round(initial[name], 5), "final_eval_loss": round(evaluate(name), 5),
+                     "last_train_loss": round(float(last[name].float()), 5), "finite": finite}
+    a, b = out["kotflash_b200"], out["sdpa_expanded"]
+    out["initial_eval_loss_abs_delta"] = round(abs(a["initial_eval_loss"] - b["initial_eval_loss"]), 6)
+    out["final_eval_loss_abs_delta"] = round(abs(a["final_eval_loss"] - b["final_eval_loss"]), 6)
+    out["speedup_vs_sdpa_expanded"] = round(b["median_step_ms"] / a["median_step_ms"], 3)
+    del models, opts
+    torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------- GPU comparator
 def bench_sdpa_comparators(dtype):
     """PyTorch SDPA's own GPU backends (cuDNN, flash, memory-efficient) on this
@@ -1187,6 +1352,7 @@ def main(argv=None) -> int:
     block = ({"fp32_projections": guarded(bench_decoder_block),
               "bf16_block": guarded(bench_decoder_block, bf16_block=True)}
              if (rank == 0 and world == 1 and not args.no_comparators) else None)
+    lm_ab = (guarded(bench_story_lm_ab) if (rank == 0 and world == 1 and not args.no_comparators) else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1205,6 +1371,8 @@ def main(argv=None) -> int:
             detail("gpu_comparators", comparators)
         if block is not None:
             detail("decoder_block_training_step", block)
+        if lm_ab is not None:
+            detail("lm_training_ab", lm_ab)
         if parity is not None and not parity.get("pass", False):
             print("parity check FAILED: " + json.dumps(parity), file=sys.stderr, flush=True)
         dec = None
