@@ -63,6 +63,10 @@ constexpr int kThreads = 384;  // 3 warpgroups: two softmax, one producer + MMA 
 // 256 * 224 + 128 * 56 = 384 * 168, the allocation the block launches with.
 constexpr int kRegSoftmax = 224, kRegOther = 56;
 constexpr int kMaxStages = 4;  // deepest K/V ring (kv_stages)
+// Epilogue staging: each softmax warp packs 16 rows x 64 columns of O (2 KB,
+// 128-byte swizzle) in shared memory and hands them to one TMA store.
+constexpr int kStoreRows = 16;
+constexpr int kStageBytes = kStoreRows * 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -198,7 +202,8 @@ __device__ __forceinline__ int round_item(int r, int n_items) {
 template <bool BF16, int NP, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-           const __grid_constant__ CUtensorMap map_v, const FwdParams p) {
+           const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+           const FwdParams p) {
   constexpr int BN = block_n(KS);             // keys per K/V block
   constexpr int STAGES = kv_stages(KS);       // K/V ring depth
   constexpr int QPANEL = kBlockM * 128;       // bytes of one 64-column panel of a 128-row Q tile
@@ -211,7 +216,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
   uint8_t* sQ = smem;                          // [2][NP][128][64]
   uint8_t* sK = sQ + 2 * QTILE;                // [STAGES][NP][BN][64]
   uint8_t* sV = sK + STAGES * KTILE;           // [STAGES][NP][BN][64]
-  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(sV + STAGES * KTILE);
+  uint8_t* sE = sV + STAGES * KTILE;           // [8 softmax warps][kStoreRows][64] epilogue staging
+  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(sE + 8 * kStageBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int d_pad16 = KS * 16;  // head dim rounded up to the MMA K step
@@ -244,6 +250,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
     kf::tma_prefetch_desc(&map_q);
     kf::tma_prefetch_desc(&map_k);
     kf::tma_prefetch_desc(&map_v);
+    kf::tma_prefetch_desc(&map_o);
   }
   kf::tc_fence_before();
   __syncthreads();
@@ -523,14 +530,17 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       }
       // -------------------------------------------------------- epilogue
       // O is read from TMEM before this thread's next p_full arrival, which
-      // is what lets the next item's first PV overwrite it.
+      // is what lets the next item's first PV overwrite it.  Rows leave
+      // through TMA stores of 16 rows x 64 columns staged in shared memory
+      // (one row per thread, 128-byte swizzle: 16-byte chunk c of staging row
+      // r sits at chunk c ^ (r & 7)); the store clips rows past Sq and
+      // columns past D.
       if (ok && (ok = __all_sync(0xffffffffu, wait_bar(&bars->o_final[t], vt & 1, bars, p.status)))) {
         kf::tc_fence_after();
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
-        const bool row_ok = row < p.Sq;
-        uint16_t* orow_g = p.o + ti.b * p.os[0] + (int64_t)my_head * p.os[1] + (int64_t)row * p.os[2];
-        // O in 64-column halves: both 32-column loads of a half are in flight
-        // before one wait (one TMEM round trip per half, not per 32 columns)
+        uint8_t* stage = sE + warp * kStageBytes;
+        const int srow = lane & (kStoreRows - 1);
+        const int row_base = my_row0 + (warp & 3) * 32;
 #pragma unroll
         for (int c0 = 0; c0 < d_pad16; c0 += 64) {
           uint32_t ov[64];
@@ -546,16 +556,26 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
 #pragma unroll
           for (int c = 0; c < 32; ++c)
             pk[c] = kf::pack2<BF16>(__uint_as_float(ov[2 * c]) * inv_l, __uint_as_float(ov[2 * c + 1]) * inv_l);
-          if (row_ok) {
 #pragma unroll
-            for (int g8 = 0; g8 < 8; ++g8) {
-              if (c0 + g8 * 8 < p.D)
-                *reinterpret_cast<uint4*>(orow_g + c0 + g8 * 8) =
-                    make_uint4(pk[4 * g8], pk[4 * g8 + 1], pk[4 * g8 + 2], pk[4 * g8 + 3]);
+          for (int half = 0; half < 32 / kStoreRows; ++half) {
+            // the previous store of this warp has read the staging rows
+            if (lane == 0) kf::bulk_wait_group_read<0>();
+            __syncwarp();
+            if (lane / kStoreRows == half) {
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch)
+                *reinterpret_cast<uint4*>(stage + srow * 128 + ((ch ^ (srow & 7)) << 4)) =
+                    make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+            }
+            kf::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              kf::tma_store_4d(&map_o, stage, c0, row_base + half * kStoreRows, my_head, ti.b);
+              kf::bulk_commit_group();
             }
           }
         }
-        if (row_ok)
+        if (row < p.Sq)
           p.lse[((int64_t)ti.b * p.Hq + my_head) * p.Sq + row] =
               l_sum > 0.f ? (m_ref + log2f(l_sum)) * kLn2 : -INFINITY;
       }
@@ -563,6 +583,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CU
       ++vt;
       if (nt == 2) jturn += nblk;
     }
+    // this warp's last O stores have written global memory
+    if (lane == 0) kf::bulk_wait_group<0>();
+    __syncwarp();
   }
 
   kf::tc_fence_before();
@@ -581,12 +604,13 @@ bool rows16(const kf_tensor4* t) {
 }
 
 template <bool BF16, int KS>
-int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
                const FwdParams& p, cudaStream_t st) {
   constexpr int NP = KS > 4 ? 2 : 1;
   constexpr size_t QTILE = (size_t)NP * kBlockM * 128;
   constexpr size_t KTILE = (size_t)NP * block_n(KS) * 128;
-  const size_t smem = 1024 + 2 * QTILE + 2 * (size_t)kv_stages(KS) * KTILE + sizeof(FwdBarriers);
+  const size_t smem = 1024 + 2 * QTILE + 2 * (size_t)kv_stages(KS) * KTILE + 8 * (size_t)kStageBytes +
+                      sizeof(FwdBarriers);
   auto kern = fwd_kernel<BF16, NP, KS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
@@ -598,22 +622,22 @@ int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
       fa.numRegs * kThreads < 256 * kRegSoftmax + 128 * kRegOther)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: register split does not fit (%d registers)", fa.numRegs);
   const int grid = std::min(p.n_items, kf::sm_count_current_device());
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, p);
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mo, p);
   return kf::check_launch("kf_attn_fwd");
 }
 
 template <bool BF16>
 int dispatch_fwd(int ks, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                 const FwdParams& p, cudaStream_t st) {
+                 const CUtensorMap& mo, const FwdParams& p, cudaStream_t st) {
   switch (ks) {
-    case 1: return launch_fwd<BF16, 1>(mq, mk, mv, p, st);
-    case 2: return launch_fwd<BF16, 2>(mq, mk, mv, p, st);
-    case 3: return launch_fwd<BF16, 3>(mq, mk, mv, p, st);
-    case 4: return launch_fwd<BF16, 4>(mq, mk, mv, p, st);
-    case 5: return launch_fwd<BF16, 5>(mq, mk, mv, p, st);
-    case 6: return launch_fwd<BF16, 6>(mq, mk, mv, p, st);
-    case 7: return launch_fwd<BF16, 7>(mq, mk, mv, p, st);
-    default: return launch_fwd<BF16, 8>(mq, mk, mv, p, st);
+    case 1: return launch_fwd<BF16, 1>(mq, mk, mv, mo, p, st);
+    case 2: return launch_fwd<BF16, 2>(mq, mk, mv, mo, p, st);
+    case 3: return launch_fwd<BF16, 3>(mq, mk, mv, mo, p, st);
+    case 4: return launch_fwd<BF16, 4>(mq, mk, mv, mo, p, st);
+    case 5: return launch_fwd<BF16, 5>(mq, mk, mv, mo, p, st);
+    case 6: return launch_fwd<BF16, 6>(mq, mk, mv, mo, p, st);
+    case 7: return launch_fwd<BF16, 7>(mq, mk, mv, mo, p, st);
+    default: return launch_fwd<BF16, 8>(mq, mk, mv, mo, p, st);
   }
 }
 
@@ -647,12 +671,13 @@ extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
   kf::DeviceGuard guard(q->ptr);
   if (guard.status()) return guard.status();
   const int box_inner = 64;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   int rc;
   if ((rc = kf::encode_tmap_4d(&mq, q, box_inner, kBlockM))) return rc;
   const int bn = block_n((int)((D + 15) / 16));
   if ((rc = kf::encode_tmap_4d(&mk, k, box_inner, bn))) return rc;
   if ((rc = kf::encode_tmap_4d(&mv, v, box_inner, bn))) return rc;
+  if ((rc = kf::encode_tmap_4d(&mo, o, box_inner, kStoreRows))) return rc;
 
   FwdParams p;
   p.o = static_cast<uint16_t*>(o->ptr);
@@ -676,6 +701,6 @@ extern "C" int kf_attn_fwd(const kf_tensor4* q, const kf_tensor4* k, const kf_te
     return set_error(KF_ERR_UNSUPPORTED, "kf_attn_fwd: grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int ks = (int)((D + 15) / 16);
-  return dtype == KF_BF16 ? dispatch_fwd<true>(ks, mq, mk, mv, p, st)
-                          : dispatch_fwd<false>(ks, mq, mk, mv, p, st);
+  return dtype == KF_BF16 ? dispatch_fwd<true>(ks, mq, mk, mv, mo, p, st)
+                          : dispatch_fwd<false>(ks, mq, mk, mv, mo, p, st);
 }

@@ -220,6 +220,16 @@ KF_DEVI void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int
       "r"(c0), "r"(c1), "r"(smem_u32(smem_src))
       : "memory");
 }
+// 4-D tiled store, this CTA's shared memory -> global (elements outside the
+// tensor are not written), tracked by the bulk-async group of the issuing
+// thread.  The writers of the tile fence it to the async proxy first.
+KF_DEVI void tma_store_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group"
+      " [%0, {%1, %2, %3, %4}], [%5];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(smem_src))
+      : "memory");
+}
 KF_DEVI void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 KF_DEVI void bulk_wait_group_read() {
