@@ -46,7 +46,11 @@
 // computes its exponentials partly on the MUFU unit and partly as a
 // polynomial on the fp32 pipe (packed f32x2 arithmetic), because 16 MUFU
 // results per clock per SM alone cannot keep up with the tensor cores at
-// head_dim 128.
+// head_dim 128.  At the end of an item each softmax warp stages its rows of
+// O (16 rows x 64 columns at a time, 16-bit, 128-byte swizzle) in its own
+// 2 KB of shared memory and one lane writes them with a TMA store.
+// Shared memory: Q tiles [2][NP][128][64], K and V rings [STAGES][NP][BN][64],
+// the eight 2 KB staging areas, then the barriers.
 #include <math.h>
 
 #include <algorithm>
