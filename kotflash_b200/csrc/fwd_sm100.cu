@@ -625,7 +625,15 @@ int launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
   if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
       fa.numRegs * kThreads < 256 * kRegSoftmax + 128 * kRegOther)
     return kf::set_error(KF_ERR_CUDA, "kf_attn_fwd: register split does not fit (%d registers)", fa.numRegs);
-  const int grid = std::min(p.n_items, kf::sm_count_current_device());
+  // A CTA that walks several items must not meet a single-tile item before a
+  // two-tile one: the tile-1 issuer skips a single-tile item without waiting,
+  // so at the next item its parity waits on the Q and K/V barriers could run
+  // two phases ahead of the producer and return at once.  Single-tile items
+  // (an odd slot count per KV head) are the first n_bh of the item order, so
+  // a launch that has them and more items than SMs gives every CTA one item.
+  const int sms = kf::sm_count_current_device();
+  const bool single_tile_items = (p.slots_per_kvh & 1) != 0;
+  const int grid = (single_tile_items && p.n_items > sms) ? p.n_items : std::min(p.n_items, sms);
   kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, mo, p);
   return kf::check_launch("kf_attn_fwd");
 }

@@ -45,6 +45,8 @@ def test_forward_reference_shapes(head_dim, causal, dtype):
         (1, 16, 4, 2048, 2048, 96, False),
         (2, 40, 40, 300, 300, 64, True),   # 160 items > 148 CTAs: persistent CTAs run several,
         (2, 40, 40, 300, 300, 64, False),  # single-tile items (odd row-block count) among them
+        (2, 80, 80, 300, 300, 64, True),   # 320 items, 160 single-tile ones first in the item order:
+        (2, 80, 80, 300, 300, 64, False),  # without one item per CTA, CTAs would meet one before a pair
     ],
 )
 def test_forward_shapes(b, hq, hkv, sq, sk, d, causal):
