@@ -26,40 +26,9 @@ import random
 
 import pytest
 
+from _sync_model import Bar, Violation, simulate
+
 STAGES = 3
-
-
-class Violation(AssertionError):
-    pass
-
-
-class Bar:
-    def __init__(self, count):
-        self.count, self.arrived, self.done = count, 0, 0
-
-    def arrive(self, n):
-        self.arrived += n
-        if self.arrived > self.count:
-            raise Violation("arrivals of two phases mixed")
-        if self.arrived == self.count:
-            self.arrived, self.done = 0, self.done + 1
-
-
-class Buf:
-    """Content tag plus the readers the content still owes."""
-
-    def __init__(self, name):
-        self.name, self.tag, self.pending = name, None, 0
-
-    def write(self, tag, readers):
-        if self.pending:
-            raise Violation(f"{self.name}: {tag} overwrites {self.tag} before its readers")
-        self.tag, self.pending = tag, readers
-
-    def read(self, tag):
-        if self.tag != tag or self.pending == 0:
-            raise Violation(f"{self.name}: read of {tag} finds {self.tag} (pending {self.pending})")
-        self.pending -= 1
 
 
 def producer(items):
@@ -156,72 +125,17 @@ def softmax(t, items, shared_s):
 
 
 def run(items, seed, shared_s=False):
-    rng = random.Random(seed)
-    bars = {"q_full": Bar(1), "q_empty": Bar(2)}
+    bars = {"q_full": Bar(1), "q_empty": Bar(2), "s_free": Bar(1)}
     for s in range(STAGES):
         bars.update({f"k_full{s}": Bar(1), f"k_empty{s}": Bar(2), f"v_full{s}": Bar(1), f"v_empty{s}": Bar(2)})
     for t in range(2):
         bars.update({f"s_full{t}": Bar(1), f"s_free{t}": Bar(1), f"p_full{t}": Bar(1), f"pv_done{t}": Bar(1),
                      f"o_final{t}": Bar(1), f"turn{t}": Bar(1)})
-    bars["s_free"] = Bar(1)
-    bufs = {}
-
-    def buf(name):
-        return bufs.setdefault(name, Buf(name))
-
     roles = {"producer": producer(items)}
     for t in range(2):
         roles[f"issuer{t}"] = issuer(t, items, shared_s)
         roles[f"softmax{t}"] = softmax(t, items, shared_s)
-    pending = {}
-    waiting = {}  # role -> (bar, m) once it started waiting
-
-    def advance(name):
-        try:
-            pending[name] = next(roles[name])
-        except StopIteration:
-            pending[name] = None
-
-    for name in roles:
-        advance(name)
-    while True:
-        live = [n for n, op in pending.items() if op is not None]
-        if not live:
-            return
-        ready = []
-        for n in live:
-            op = pending[n]
-            if op[0] != "wait":
-                ready.append(n)
-                continue
-            b, m = bars[op[1]], op[2]
-            if n not in waiting:
-                if not (m <= b.done <= m + 1):
-                    raise Violation(f"{n} waits for completion {m} of {op[1]} at {b.done}")
-                waiting[n] = (op[1], m)
-            if b.done > m:
-                ready.append(n)
-        if not ready:
-            raise Violation("deadlock: " + ", ".join(f"{n}: {pending[n]}" for n in live))
-        n = rng.choice(ready)
-        op = pending[n]
-        kind = op[0]
-        if kind == "wait":
-            waiting.pop(n, None)
-        elif kind == "arrive":
-            b = bars[op[1]]
-            b.arrive(op[2])
-            for w, (bn, m) in waiting.items():
-                if bn == op[1] and b.done >= m + 2:
-                    raise Violation(f"{w} still waits for completion {m} of {bn} at {b.done}")
-        elif kind == "write":
-            buf(op[1]).write(op[2], op[3])
-        elif kind == "read":
-            buf(op[1]).read(op[2])
-        elif kind == "read_write":
-            buf(op[1]).read(op[2])
-            buf(op[1]).write(op[3], 1)
-        advance(n)
+    simulate(roles, bars, seed)
 
 
 def random_items(rng, n, tiles=(2,)):
