@@ -52,8 +52,20 @@ def producer(items):
         g += nblk
 
 
+def content_order(items):
+    """(tile, that tile's load index) of every S content, in issue order."""
+    order, loads = [], [0, 0]
+    for nt, nblk in items:
+        for j in range(nblk):
+            for t in range(nt):
+                order.append((t, loads[t]))
+                loads[t] += 1
+    return order
+
+
 def issuer(t, items, shared_s):
     g = jt = cs = 0
+    contents = content_order(items)
     for it, (nt, nblk) in enumerate(items):
         if t < nt:
             rel = 1 if nt == 2 else 2
@@ -63,7 +75,13 @@ def issuer(t, items, shared_s):
                 if not shared_s:
                     return [] if j == 0 else [("wait", f"s_free{t}", jt + j - 1)]
                 c = cs + (2 * j + t if nt == 2 else j)
-                return [] if c == 0 else [("wait", "s_free", c - 1)]
+                if c == 0:
+                    return []
+                if shared_s == "per_tile":
+                    # wait for the load of content c - 1 on the barrier of the tile that loaded it
+                    owner, index = contents[c - 1]
+                    return [("wait", f"s_free{owner}", index)]
+                return [("wait", "s_free", c - 1)]
 
             def qk(j, gj):
                 s = gj % STAGES
@@ -107,7 +125,7 @@ def softmax(t, items, shared_s):
         for j in range(nblk):
             yield ("wait", f"s_full{t}", jt + j)
             yield ("read", sbuf, (it, t, j))
-            yield ("arrive", "s_free" if shared_s else f"s_free{t}", 1)
+            yield ("arrive", "s_free" if shared_s is True else f"s_free{t}", 1)
             if nt == 2 and (t == 1 or j > 0):
                 yield ("wait", f"turn{t}", jturn + j - (0 if t == 1 else 1))
             if nt == 2:
@@ -193,6 +211,18 @@ def test_shared_score_buffer_breaks_the_parity_invariant():
             except Violation:
                 failures += 1
     assert failures > 0
+
+
+def test_shared_score_buffer_with_a_load_barrier_per_tile_passes():
+    """The repaired form of the shared-buffer variant: each tile's softmax
+    arrives on its own load barrier, and the issuer of content c waits for
+    the load of content c - 1 on the barrier of the tile that loaded it (a
+    waiter is then never two phases ahead of that barrier)."""
+    rng = random.Random(12)
+    for case in range(40):
+        items = random_items(rng, rng.randint(1, 4))
+        for seed in range(15):
+            run(items, seed=1000 * case + seed, shared_s="per_tile")
 
 
 def test_model_catches_a_missing_wait():
